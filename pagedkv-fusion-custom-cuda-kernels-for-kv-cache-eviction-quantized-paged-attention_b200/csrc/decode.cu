@@ -1,0 +1,835 @@
+// INT8 paged decode attention for sm_100a: split-K over pages plus a
+// cross-split combine.
+//
+// Semantics follow pagedkv_fusion/reference.py:117-173 (decode step, one
+// query token per sequence, per-(block, head) INT8 scales, GQA by
+// kv_head = h / (H / Hkv)).  The launcher contract mirrors
+// csrc/quant_paged_attention.cu:172-225 of the reference (same argument
+// meaning and shape checks); a sequence of length 0 produces zeros.
+//
+// Two kernels do the streaming work:
+//
+//  * decode_fast_kernel  (head_dim 128, block_size 16/32, H/Hkv a power of
+//    two <= 8).  One CTA = one (sequence, split of pages, group of HG KV
+//    heads).  A producer warp streams each page's [block_size x HG x 128]
+//    int8 tile with one TMA (cp.async.bulk.tensor, 128-byte swizzle) into a
+//    4-stage ring guarded by mbarriers; 8 consumer warps compute.  K pages
+//    of the split are streamed first, then V pages, so the softmax of a
+//    split needs one barrier and no rescaling.  q.k uses IDP4A: the fp32
+//    query is written as a 24-bit fixed-point integer split into three
+//    signed 8-bit digits, so each 4-byte K word costs three integer dot
+//    products and no int8->float conversion.  p.V converts V bytes with a
+//    byte-permute into the mantissa of 2^23 and one float subtract.
+//
+//  * decode_generic_kernel  (any head_dim % 32 == 0 <= 256, block_size <=
+//    64, any group size): plain loads, one CTA per (sequence, split, query
+//    head).
+//
+// Logits are kept pre-multiplied by log2(e) so the softmax uses exp2; each
+// split writes (m, l, acc[D]) and decode_combine_kernel merges splits.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "pkv_common.cuh"
+#include "pkv_internal.h"
+
+namespace pkv {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kQFix = 127 * 65536;  // largest |integer| of the 3-digit query
+
+// ===========================================================================
+// Tensor maps for the paged caches
+// ===========================================================================
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// View the cache [NB, BS, Hkv, 128] int8 as a 3-D tensor (d, kv_head,
+// token row) and load boxes of (128, hg, BS).
+bool make_cache_map(CUtensorMap* map, const int8_t* cache, int64_t num_blocks, int bs,
+                    int hkv, int hg) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {128, (cuuint64_t)hkv, (cuuint64_t)(num_blocks * bs)};
+  cuuint64_t strides[2] = {128, (cuuint64_t)hkv * 128};
+  cuuint32_t box[3] = {128, (cuuint32_t)hg, (cuuint32_t)bs};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(cache), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Small cache of encoded maps: a serving loop calls decode with the same
+// cache tensors every step.
+struct MapKey {
+  const void* ptr;
+  int64_t nb;
+  int bs, hkv, hg;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && nb == o.nb && bs == o.bs && hkv == o.hkv && hg == o.hg;
+  }
+};
+
+bool cached_cache_map(CUtensorMap* out, const int8_t* cache, int64_t nb, int bs, int hkv,
+                      int hg) {
+  static std::mutex mu;
+  static MapKey keys[16];
+  static CUtensorMap maps[16];
+  static int used = 0, next = 0;
+  MapKey key{cache, nb, bs, hkv, hg};
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (keys[i] == key) {
+      *out = maps[i];
+      return true;
+    }
+  if (!make_cache_map(out, cache, nb, bs, hkv, hg)) return false;
+  keys[next] = key;
+  maps[next] = *out;
+  next = (next + 1) % 16;
+  used = std::min(used + 1, 16);
+  return true;
+}
+
+// ===========================================================================
+// Small device helpers
+// ===========================================================================
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Balanced base-256 digits of an integer |n| <= 127*65536: n = d2*65536 +
+// d1*256 + d0 with every digit in [-128, 127].
+__device__ __forceinline__ void to_digits(int n, int& d0, int& d1, int& d2) {
+  d0 = ((n + 128) & 255) - 128;
+  const int n1 = (n - d0) >> 8;
+  d1 = ((n1 + 128) & 255) - 128;
+  d2 = (n1 - d1) >> 8;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) |
+         ((uint32_t)(d & 255) << 24);
+}
+
+// int8 byte i of w -> float, exactly: the biased byte becomes the low
+// mantissa bits of 2^23, and the bias is subtracted in one float op.
+__device__ __forceinline__ void bytes_to_float4(uint32_t w, float& f0, float& f1, float& f2,
+                                                float& f3) {
+  const uint32_t u = w ^ 0x80808080u;
+  f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
+  f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
+  f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
+  f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// ===========================================================================
+// Fast kernel
+// ===========================================================================
+
+constexpr int kFastStages = 4;
+constexpr int kStageBytes = 128 * 128;  // 128 cache lines of 128 B
+constexpr int kMaxTok = 512;            // tokens per split
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kFastThreads = kConsumers + 32;
+
+template <int BS, int HG, int G>
+struct FastCfg {
+  static constexpr int kLinesPerPage = BS * HG;
+  static_assert(128 % kLinesPerPage == 0 && kLinesPerPage >= 8, "page tile shape");
+  static constexpr int kPPS = 128 / kLinesPerPage;  // pages per stage
+  static constexpr int kPageBytes = kLinesPerPage * 128;
+  static constexpr int kTokPerStage = kPPS * BS;
+  static constexpr int kMaxPages = kMaxTok / BS;
+  static constexpr int kNHG = HG * G;  // query heads handled by one CTA
+  static_assert(kNHG <= 16, "query heads per CTA");
+  static constexpr int kR = kConsumerWarps / HG;  // token slices in the V phase
+  static constexpr int kQdStride = 3 * 128 + 16;  // padded: spreads banks
+  static constexpr int kOffLogit = kFastStages * kStageBytes;
+  static constexpr int kOffQd = kOffLogit + kNHG * kMaxTok * 4;
+  static constexpr int kOffQs = kOffQd + (G > 1 ? kNHG * kQdStride : 0);
+  static constexpr int kOffMl = kOffQs + 64;
+  static constexpr int kOffPhys = kOffMl + 16 * 8;
+  static constexpr int kOffKs = kOffPhys + kMaxPages * 4;
+  static constexpr int kOffVs = kOffKs + kMaxPages * HG * 4;
+  static constexpr int kOffBar = ((kOffVs + kMaxPages * HG * 4) + 15) & ~15;
+  static constexpr int kOffFlag = kOffBar + 2 * kFastStages * 8;
+  static constexpr int kSmemBytes = kOffFlag + 16 + 1024;  // + alignment slack
+};
+
+template <int BS, int HG, int G>
+__global__ void __launch_bounds__(kFastThreads, 2)
+    decode_fast_kernel(const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q,
+                       const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+                       const int32_t* __restrict__ block_tables,
+                       const int32_t* __restrict__ seq_lens, float* __restrict__ out,
+                       float* __restrict__ ws_acc, float2* __restrict__ ws_ml, int num_heads,
+                       int num_kv_heads, int64_t num_blocks, int max_blocks_per_seq,
+                       float qk_scale, int pages_per_split, int max_splits, int* err) {
+  using C = FastCfg<BS, HG, G>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* s_logit = reinterpret_cast<float*>(smem + C::kOffLogit);
+  float* s_qs = reinterpret_cast<float*>(smem + C::kOffQs);
+  float2* s_ml = reinterpret_cast<float2*>(smem + C::kOffMl);
+  int* s_phys = reinterpret_cast<int*>(smem + C::kOffPhys);
+  float* s_ks = reinterpret_cast<float*>(smem + C::kOffKs);
+  float* s_vs = reinterpret_cast<float*>(smem + C::kOffVs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + kFastStages;
+  const uint32_t stage_base = smem_u32(smem);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int seq = blockIdx.x;
+  const int split = blockIdx.y;
+  const int j0 = blockIdx.z * HG;  // first KV head of this CTA
+
+  const int L = seq_lens[seq];
+  const int n_pages = (L + BS - 1) / BS;
+  const int p0 = split * pages_per_split;
+  if (p0 >= n_pages) return;  // uniform across the CTA
+  const int np = min(n_pages - p0, pages_per_split);
+  const int t_begin = p0 * BS;
+  const int T = min(L, (p0 + np) * BS) - t_begin;
+  const int n_stages = (np + C::kPPS - 1) / C::kPPS;
+  const int n_splits = (n_pages + pages_per_split - 1) / pages_per_split;
+
+  // ---- prologue: block table, scales, query digits -----------------------
+  const int32_t* bt_row = block_tables + (int64_t)seq * max_blocks_per_seq + p0;
+  for (int i = tid; i < np * HG; i += kFastThreads) {
+    const int pg = i / HG, jj = i - pg * HG;
+    const int phys = bt_row[pg];
+    const bool ok = phys >= 0 && (int64_t)phys < num_blocks;
+    if (jj == 0) {
+      s_phys[pg] = ok ? phys : -1;
+      if (!ok) record_error(err, kDevBadBlockId);
+    }
+    const int64_t si = (int64_t)(ok ? phys : 0) * num_kv_heads + j0 + jj;
+    s_ks[i] = ok ? k_scale[si] : 0.0f;
+    s_vs[i] = ok ? v_scale[si] : 0.0f;
+  }
+
+  // query digits: for G == 1 every consumer keeps its own slice in
+  // registers; for G > 1 they live in shared memory.
+  uint4 qd[4][3];
+  float my_qs = 0.0f;
+  const int k_line = tid >> 1;  // K phase: two threads per cache line
+  const int k_half = tid & 1;
+  const int k_jj = k_line % HG;
+  if constexpr (G == 1) {
+    if (warp < kConsumerWarps) {
+      const float4* qrow = reinterpret_cast<const float4*>(
+          q + ((int64_t)seq * num_heads + (j0 + k_jj)) * 128 + k_half * 64);
+      float4 v[16];
+      float m = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v[i] = qrow[i];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)),
+                           fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+      }
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      const float inv = m > 0.0f ? (float)kQFix / m : 0.0f;
+      my_qs = m > 0.0f ? m / (float)kQFix : 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t w[3][4];
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const float4 x = v[c * 4 + wi];
+          int d[4][3];
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            int n = __float2int_rn(xs[e] * inv);
+            n = max(-kQFix, min(kQFix, n));
+            to_digits(n, d[e][0], d[e][1], d[e][2]);
+          }
+#pragma unroll
+          for (int j = 0; j < 3; ++j) w[j][wi] = pack4(d[0][j], d[1][j], d[2][j], d[3][j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 3; ++j) qd[c][j] = make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
+      }
+    }
+  } else {
+    uint8_t* s_qd = smem + C::kOffQd;
+    for (int hg = warp; hg < C::kNHG; hg += kConsumerWarps + 1) {
+      const int hq = (j0 + hg / G) * G + hg % G;
+      const float4 x = reinterpret_cast<const float4*>(
+          q + ((int64_t)seq * num_heads + hq) * 128)[lane];
+      float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+      m = warp_max(m);
+      const float inv = m > 0.0f ? (float)kQFix / m : 0.0f;
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+      int d[4][3];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int n = __float2int_rn(xs[e] * inv);
+        n = max(-kQFix, min(kQFix, n));
+        to_digits(n, d[e][0], d[e][1], d[e][2]);
+      }
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        reinterpret_cast<uint32_t*>(s_qd + hg * C::kQdStride + j * 128)[lane] =
+            pack4(d[0][j], d[1][j], d[2][j], d[3][j]);
+      if (lane == 0) s_qs[hg] = m > 0.0f ? m / (float)kQFix : 0.0f;
+    }
+  }
+
+  if (tid == 0) {
+    for (int s = 0; s < kFastStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  // ---- producer warp -----------------------------------------------------
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+      const uint64_t policy = l2_policy_evict_first();
+      const int total = 2 * n_stages;
+      for (int i = 0; i < total; ++i) {
+        const int slot = i % kFastStages;
+        const uint32_t ph = (uint32_t)(i / kFastStages) & 1u;
+        if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          break;
+        }
+        const bool is_v = i >= n_stages;
+        const int st = is_v ? i - n_stages : i;
+        const int pb = st * C::kPPS;
+        const int pe = min(np, pb + C::kPPS);
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)((pe - pb) * C::kPageBytes));
+        for (int pg = pb; pg < pe; ++pg) {
+          const int phys = max(s_phys[pg], 0);
+          tma_load_3d(smem + slot * kStageBytes + (pg - pb) * C::kPageBytes,
+                      is_v ? &map_v : &map_k, &full[slot], 0, j0, phys * BS, policy);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- consumers: K phase -------------------------------------------------
+  bool live = true;
+  for (int st = 0; st < n_stages; ++st) {
+    const int slot = st % kFastStages;
+    const uint32_t ph = (uint32_t)(st / kFastStages) & 1u;
+    if (live && !mbar_wait_bounded(&full[slot], ph, err)) {
+      record_error(err, kDevWaitTimeout);
+      live = false;
+    }
+    if (live) {
+      const int tok = st * C::kTokPerStage + k_line / HG;
+      const uint32_t line_addr = stage_base + slot * kStageBytes + k_line * 128;
+      int acc[G][3];
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = 0;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c = k_half * 4 + cc;
+        const uint4 kw = lds128(line_addr + ((c ^ (k_line & 7)) << 4));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            uint4 qw;
+            if constexpr (G == 1) {
+              qw = qd[cc][j];
+            } else {
+              qw = lds128(smem_u32(smem + C::kOffQd + (k_jj * G + g) * C::kQdStride + j * 128 +
+                                   c * 16));
+            }
+            int a = acc[g][j];
+            a = __dp4a((int)kw.x, (int)qw.x, a);
+            a = __dp4a((int)kw.y, (int)qw.y, a);
+            a = __dp4a((int)kw.z, (int)qw.z, a);
+            a = __dp4a((int)kw.w, (int)qw.w, a);
+            acc[g][j] = a;
+          }
+        }
+      }
+      const int pg = tok / BS;
+      const bool valid = tok < T && s_phys[pg] >= 0;
+      const float ks = s_ks[pg * HG + k_jj];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float part = (float)acc[g][2] * 65536.0f + ((float)acc[g][1] * 256.0f + (float)acc[g][0]);
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        const float qs = (G == 1) ? my_qs : s_qs[k_jj * G + g];
+        if (k_half == 0 && tok < T)
+          s_logit[(k_jj * G + g) * kMaxTok + tok] = valid ? part * (qs * ks * qk_scale) : -INFINITY;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  named_barrier(1, kConsumers);
+
+  // ---- softmax over the split (per query head) ---------------------------
+  for (int hg = warp; hg < C::kNHG; hg += kConsumerWarps) {
+    float* row = s_logit + hg * kMaxTok;
+    float m = -INFINITY;
+    for (int t = lane; t < T; t += 32) m = fmaxf(m, row[t]);
+    m = warp_max(m);
+    const int jj = hg / G;
+    float l = 0.0f;
+    for (int t = lane; t < T; t += 32) {
+      const float p = (m == -INFINITY) ? 0.0f : exp2f(row[t] - m);
+      l += p;
+      row[t] = p * s_vs[(t / BS) * HG + jj];
+    }
+    l = warp_sum(l);
+    if (lane == 0) s_ml[hg] = make_float2(m, l);
+  }
+  named_barrier(1, kConsumers);
+
+  // ---- V phase -------------------------------------------------------------
+  const int v_jj = warp % HG;
+  const int v_r = warp / HG;
+  float acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
+  const uint32_t word_off = (uint32_t)((lane & 3) << 2);
+  const int chunk = lane >> 2;
+  for (int st = 0; st < n_stages; ++st) {
+    const int i = n_stages + st;
+    const int slot = i % kFastStages;
+    const uint32_t ph = (uint32_t)(i / kFastStages) & 1u;
+    if (live && !mbar_wait_bounded(&full[slot], ph, err)) {
+      record_error(err, kDevWaitTimeout);
+      live = false;
+    }
+    if (live) {
+      const uint32_t base = stage_base + slot * kStageBytes;
+      const int tok0 = st * C::kTokPerStage;
+      const int tcount = min(C::kTokPerStage, T - tok0);
+#pragma unroll 4
+      for (int ts = v_r; ts < tcount; ts += C::kR) {
+        const int line = ts * HG + v_jj;
+        const uint32_t w = lds32(base + line * 128 + ((chunk ^ (line & 7)) << 4) + word_off);
+        float f0, f1, f2, f3;
+        bytes_to_float4(w, f0, f1, f2, f3);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float p = s_logit[(v_jj * G + g) * kMaxTok + tok0 + ts];
+          acc[g][0] = fmaf(p, f0, acc[g][0]);
+          acc[g][1] = fmaf(p, f1, acc[g][1]);
+          acc[g][2] = fmaf(p, f2, acc[g][2]);
+          acc[g][3] = fmaf(p, f3, acc[g][3]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+
+  // ---- reduce token slices, then write -------------------------------------
+  if constexpr (C::kR > 1) {
+    named_barrier(1, kConsumers);  // every stage consumed: the ring is free
+    float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      reinterpret_cast<float4*>(red + ((v_r * HG + v_jj) * G + g) * 128)[lane] =
+          make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    named_barrier(1, kConsumers);
+    if (v_r == 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        for (int r = 1; r < C::kR; ++r) {
+          const float4 o =
+              reinterpret_cast<const float4*>(red + ((r * HG + v_jj) * G + g) * 128)[lane];
+          acc[g][0] += o.x;
+          acc[g][1] += o.y;
+          acc[g][2] += o.z;
+          acc[g][3] += o.w;
+        }
+      }
+    }
+  }
+  if (v_r == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int hg = v_jj * G + g;
+      const int hq = (j0 + v_jj) * G + g;
+      const float2 ml = s_ml[hg];
+      if (n_splits == 1) {
+        const float inv = ml.y > 0.0f ? 1.0f / ml.y : 0.0f;
+        reinterpret_cast<float4*>(out + ((int64_t)seq * num_heads + hq) * 128)[lane] =
+            make_float4(acc[g][0] * inv, acc[g][1] * inv, acc[g][2] * inv, acc[g][3] * inv);
+      } else {
+        const int64_t slot = ((int64_t)seq * max_splits + split) * num_heads + hq;
+        reinterpret_cast<float4*>(ws_acc + slot * 128)[lane] =
+            make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+        if (lane == 0) ws_ml[slot] = ml;
+      }
+    }
+  }
+}
+
+// ===========================================================================
+// Generic kernel
+// ===========================================================================
+
+constexpr int kGenThreads = 128;
+constexpr int kGenMaxTok = 2048;
+
+__global__ void __launch_bounds__(kGenThreads)
+    decode_generic_kernel(const float* __restrict__ q, const int8_t* __restrict__ k_cache,
+                          const float* __restrict__ k_scale, const int8_t* __restrict__ v_cache,
+                          const float* __restrict__ v_scale,
+                          const int32_t* __restrict__ block_tables,
+                          const int32_t* __restrict__ seq_lens, float* __restrict__ out,
+                          float* __restrict__ ws_acc, float2* __restrict__ ws_ml, int num_heads,
+                          int num_kv_heads, int head_dim, int bs, int64_t num_blocks,
+                          int max_blocks_per_seq, float qk_scale, int pages_per_split,
+                          int max_splits, int* err) {
+  __shared__ float s_q[256];
+  __shared__ float s_p[kGenMaxTok];
+  __shared__ float s_red[kGenThreads / 32];
+  const int seq = blockIdx.x;
+  const int split = blockIdx.y;
+  const int h = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int L = seq_lens[seq];
+  const int n_pages = (L + bs - 1) / bs;
+  const int p0 = split * pages_per_split;
+  if (p0 >= n_pages) return;
+  const int np = min(n_pages - p0, pages_per_split);
+  const int t_begin = p0 * bs;
+  const int T = min(L, (p0 + np) * bs) - t_begin;
+  const int n_splits = (n_pages + pages_per_split - 1) / pages_per_split;
+  const int kvh = h / (num_heads / num_kv_heads);
+  const int32_t* bt_row = block_tables + (int64_t)seq * max_blocks_per_seq;
+  const int64_t row_stride = (int64_t)num_kv_heads * head_dim;
+
+  for (int d = tid; d < head_dim; d += kGenThreads)
+    s_q[d] = q[((int64_t)seq * num_heads + h) * head_dim + d];
+  __syncthreads();
+
+  // logits: one warp per token
+  for (int t = warp; t < T; t += kGenThreads / 32) {
+    const int pos = t_begin + t;
+    const int phys = bt_row[pos / bs];
+    const bool ok = phys >= 0 && (int64_t)phys < num_blocks;
+    float dot = 0.0f;
+    if (ok) {
+      const int8_t* kr = k_cache + ((int64_t)phys * bs + pos % bs) * row_stride +
+                         (int64_t)kvh * head_dim;
+      for (int d = lane; d < head_dim; d += 32) dot = fmaf(s_q[d], (float)kr[d], dot);
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) {
+      if (!ok) record_error(err, kDevBadBlockId);
+      s_p[t] = ok ? dot * (k_scale[(int64_t)phys * num_kv_heads + kvh] * qk_scale) : -INFINITY;
+    }
+  }
+  __syncthreads();
+
+  float m = -INFINITY;
+  for (int t = tid; t < T; t += kGenThreads) m = fmaxf(m, s_p[t]);
+  m = warp_max(m);
+  if (lane == 0) s_red[warp] = m;
+  __syncthreads();
+  m = s_red[0];
+  for (int w = 1; w < kGenThreads / 32; ++w) m = fmaxf(m, s_red[w]);
+  __syncthreads();
+  float l = 0.0f;
+  for (int t = tid; t < T; t += kGenThreads) {
+    const float p = (m == -INFINITY) ? 0.0f : exp2f(s_p[t] - m);
+    s_p[t] = p;
+    l += p;
+  }
+  l = warp_sum(l);
+  if (lane == 0) s_red[warp] = l;
+  __syncthreads();
+  l = 0.0f;
+  for (int w = 0; w < kGenThreads / 32; ++w) l += s_red[w];
+
+  for (int d = tid; d < head_dim; d += kGenThreads) {
+    float acc = 0.0f;
+    for (int t = 0; t < T; ++t) {
+      const int pos = t_begin + t;
+      const int phys = bt_row[pos / bs];
+      if (phys < 0 || (int64_t)phys >= num_blocks) continue;
+      const float vs = v_scale[(int64_t)phys * num_kv_heads + kvh];
+      const int8_t* vr = v_cache + ((int64_t)phys * bs + pos % bs) * row_stride +
+                         (int64_t)kvh * head_dim;
+      acc = fmaf(s_p[t] * vs, (float)vr[d], acc);
+    }
+    if (n_splits == 1) {
+      out[((int64_t)seq * num_heads + h) * head_dim + d] = l > 0.0f ? acc / l : 0.0f;
+    } else {
+      const int64_t slot = ((int64_t)seq * max_splits + split) * num_heads + h;
+      ws_acc[slot * head_dim + d] = acc;
+      if (d == 0) ws_ml[slot] = make_float2(m, l);
+    }
+  }
+}
+
+// ===========================================================================
+// Combine
+// ===========================================================================
+
+__global__ void __launch_bounds__(128)
+    decode_combine_kernel(const int32_t* __restrict__ seq_lens, const float* __restrict__ ws_acc,
+                          const float2* __restrict__ ws_ml, float* __restrict__ out,
+                          int num_heads, int head_dim, int bs, int pages_per_split,
+                          int max_splits) {
+  const int seq = blockIdx.x;
+  const int h = blockIdx.y;
+  const int L = seq_lens[seq];
+  const int n_pages = (L + bs - 1) / bs;
+  const int n_splits = (n_pages + pages_per_split - 1) / pages_per_split;
+  float* o = out + ((int64_t)seq * num_heads + h) * head_dim;
+  if (n_splits == 0) {
+    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) o[d] = 0.0f;
+    return;
+  }
+  if (n_splits == 1) return;  // written by the split kernel
+  const int64_t base = (int64_t)seq * max_splits * num_heads + h;
+  float M = -INFINITY;
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, ws_ml[base + (int64_t)s * num_heads].x);
+  float denom = 0.0f;
+  for (int s = 0; s < n_splits; ++s) {
+    const float2 ml = ws_ml[base + (int64_t)s * num_heads];
+    if (ml.x != -INFINITY) denom += exp2f(ml.x - M) * ml.y;
+  }
+  const float inv = denom > 0.0f ? 1.0f / denom : 0.0f;
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float acc = 0.0f;
+    for (int s = 0; s < n_splits; ++s) {
+      const int64_t slot = base + (int64_t)s * num_heads;
+      const float mx = ws_ml[slot].x;
+      if (mx != -INFINITY) acc += exp2f(mx - M) * ws_acc[slot * head_dim + d];
+    }
+    o[d] = acc * inv;
+  }
+}
+
+// ===========================================================================
+// Planning and dispatch
+// ===========================================================================
+
+struct Plan {
+  bool fast = false;
+  int hg = 1, g = 1;
+  int pages_per_split = 1;
+  int max_splits = 1;
+};
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+int largest_pow2_divisor_upto(int n, int cap) {
+  int r = 1;
+  while (r * 2 <= cap && n % (r * 2) == 0) r *= 2;
+  return r;
+}
+
+Plan make_plan(const DecodeArgs& a) {
+  Plan p;
+  const int group = a.num_heads / a.num_kv_heads;
+  const bool g_ok = group >= 1 && group <= 8 && (group & (group - 1)) == 0;
+  const bool aligned = (reinterpret_cast<uintptr_t>(a.k_cache) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(a.v_cache) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(a.q) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(a.out) % 16 == 0);
+  p.fast = a.head_dim == 128 && (a.block_size == 16 || a.block_size == 32) && g_ok && aligned &&
+           (int64_t)a.num_blocks * a.block_size < (int64_t)1 << 31 && env_int("PKV_DECODE_GENERIC", 0) == 0;
+  const int M = a.max_blocks_per_seq;
+  if (p.fast) {
+    p.g = group;
+    const int cap = std::min(128 / a.block_size, 16 / group);
+    p.hg = largest_pow2_divisor_upto(a.num_kv_heads, std::min(8, cap));
+    if (a.block_size * p.hg < 8) p.fast = false;
+  }
+  if (p.fast) {
+    const int pps_stage = 128 / (a.block_size * p.hg);
+    const int max_pages = kMaxTok / a.block_size;
+    const int groups = a.num_kv_heads / p.hg;
+    int pps = max_pages;
+    const int64_t target = env_int("PKV_DECODE_TARGET_CTAS", 888);
+    while (pps > pps_stage && (int64_t)a.num_seqs * groups * ((M + pps - 1) / pps) < target)
+      pps /= 2;
+    const int forced = env_int("PKV_DECODE_SPLIT_PAGES", 0);
+    if (forced > 0) pps = std::max(pps_stage, std::min(max_pages, forced / pps_stage * pps_stage));
+    p.pages_per_split = std::max(pps, pps_stage);
+  } else {
+    const int max_pages = std::max(1, kGenMaxTok / a.block_size);
+    int pps = max_pages;
+    while (pps > 1 && (int64_t)a.num_seqs * a.num_heads * ((M + pps - 1) / pps) < 888) pps /= 2;
+    p.pages_per_split = pps;
+  }
+  p.max_splits = std::max(1, (M + p.pages_per_split - 1) / p.pages_per_split);
+  return p;
+}
+
+template <int BS, int HG, int G>
+int launch_fast_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_ml,
+                  cudaStream_t stream) {
+  using C = FastCfg<BS, HG, G>;
+  CUtensorMap mk, mv;
+  if (!cached_cache_map(&mk, a.k_cache, a.num_blocks, BS, a.num_kv_heads, HG) ||
+      !cached_cache_map(&mv, a.v_cache, a.num_blocks, BS, a.num_kv_heads, HG)) {
+    set_error("cuTensorMapEncodeTiled failed for the paged cache");
+    return kCudaError;
+  }
+  auto kern = decode_fast_kernel<BS, HG, G>;
+  static bool attr_done = false;  // per instantiation
+  if (!attr_done) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    attr_done = true;
+  }
+  dim3 grid(a.num_seqs, p.max_splits, a.num_kv_heads / HG);
+  kern<<<grid, kFastThreads, C::kSmemBytes, stream>>>(
+      mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out, ws_acc, ws_ml,
+      a.num_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq, a.sm_scale * kLog2e,
+      p.pages_per_split, p.max_splits, device_error_word());
+  return kOk;
+}
+
+template <int BS, int HG>
+int dispatch_g(const DecodeArgs& a, const Plan& p, float* wa, float2* wm, cudaStream_t s) {
+  switch (p.g) {
+    case 1: return launch_fast_t<BS, HG, 1>(a, p, wa, wm, s);
+    case 2: if constexpr (HG * 2 <= 16) return launch_fast_t<BS, HG, 2>(a, p, wa, wm, s); break;
+    case 4: if constexpr (HG * 4 <= 16) return launch_fast_t<BS, HG, 4>(a, p, wa, wm, s); break;
+    case 8: if constexpr (HG * 8 <= 16) return launch_fast_t<BS, HG, 8>(a, p, wa, wm, s); break;
+  }
+  set_error("internal: no fast decode instantiation for this group size");
+  return kUnsupported;
+}
+
+template <int BS>
+int dispatch_hg(const DecodeArgs& a, const Plan& p, float* wa, float2* wm, cudaStream_t s) {
+  switch (p.hg) {
+    case 1: return dispatch_g<BS, 1>(a, p, wa, wm, s);
+    case 2: return dispatch_g<BS, 2>(a, p, wa, wm, s);
+    case 4: return dispatch_g<BS, 4>(a, p, wa, wm, s);
+    case 8: if constexpr (BS * 8 <= 128) return dispatch_g<BS, 8>(a, p, wa, wm, s); break;
+  }
+  set_error("internal: no fast decode instantiation for this head grouping");
+  return kUnsupported;
+}
+
+}  // namespace
+
+size_t decode_workspace_size(const DecodeArgs& a) {
+  const Plan p = make_plan(a);
+  if (p.max_splits <= 1) return 0;
+  const size_t slots = (size_t)a.num_seqs * p.max_splits * a.num_heads;
+  return slots * a.head_dim * sizeof(float) + slots * sizeof(float2) + 256;
+}
+
+int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
+                  cudaStream_t stream) {
+  if (a.num_seqs == 0) return kOk;
+  const Plan p = make_plan(a);
+  float* ws_acc = nullptr;
+  float2* ws_ml = nullptr;
+  if (p.max_splits > 1) {
+    const size_t need = decode_workspace_size(a);
+    if (workspace == nullptr || workspace_bytes < need) {
+      set_error("workspace too small for split-K decode: need " + std::to_string(need) +
+                " bytes");
+      return kWorkspace;
+    }
+    uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
+    const size_t slots = (size_t)a.num_seqs * p.max_splits * a.num_heads;
+    ws_acc = reinterpret_cast<float*>(base);
+    ws_ml = reinterpret_cast<float2*>(base + slots * a.head_dim * sizeof(float));
+  }
+  int rc = kOk;
+  if (p.fast) {
+    rc = a.block_size == 16 ? dispatch_hg<16>(a, p, ws_acc, ws_ml, stream)
+                            : dispatch_hg<32>(a, p, ws_acc, ws_ml, stream);
+  } else {
+    dim3 grid(a.num_seqs, p.max_splits, a.num_heads);
+    decode_generic_kernel<<<grid, kGenThreads, 0, stream>>>(
+        a.q, a.k_cache, a.k_scale, a.v_cache, a.v_scale, a.block_tables, a.seq_lens, a.out,
+        ws_acc, ws_ml, a.num_heads, a.num_kv_heads, a.head_dim, a.block_size, a.num_blocks,
+        a.max_blocks_per_seq, a.sm_scale * kLog2e, p.pages_per_split, p.max_splits,
+        device_error_word());
+  }
+  if (rc != kOk) return rc;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("decode launch failed: ") + cudaGetErrorString(e));
+    return kCudaError;
+  }
+  // Splits > 1 and empty sequences are finished by the combine.
+  dim3 cgrid(a.num_seqs, a.num_heads);
+  decode_combine_kernel<<<cgrid, 128, 0, stream>>>(a.seq_lens, ws_acc, ws_ml, a.out, a.num_heads,
+                                                   a.head_dim, a.block_size, p.pages_per_split,
+                                                   p.max_splits);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string("combine launch failed: ") + cudaGetErrorString(e));
+    return kCudaError;
+  }
+  return kOk;
+}
+
+}  // namespace pkv

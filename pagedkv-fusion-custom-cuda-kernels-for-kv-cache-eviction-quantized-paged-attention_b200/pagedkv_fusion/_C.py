@@ -1,0 +1,287 @@
+"""``pagedkv_fusion._C`` -- the native boundary, bound with ctypes.
+
+Drop-in for the reference's pybind11 module (csrc/bindings.cpp:14-26): the
+same two functions with the same argument names, defaults and error type
+(``RuntimeError`` where the reference's ``TORCH_CHECK`` raises), plus the
+entry points this build adds (native quantizer, deterministic selection,
+sharded-eviction candidates and merge, cache writer).  Every function takes
+CUDA tensors, allocates its outputs with torch's caching allocator on the
+input's device, and enqueues work on that device's current stream without
+synchronizing -- as the reference launcher does (quant_paged_attention.cu:
+207-223).  The arithmetic happens in ``lib/libpagedkv_sm100.so``; importing
+this module fails with ``ImportError`` when that library has not been built.
+"""
+
+from __future__ import annotations
+
+import ctypes as ct
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent / "lib" / "libpagedkv_sm100.so"
+if not _LIB_PATH.exists():
+    raise ImportError(f"{_LIB_PATH} is not built (run build.py in the package root)")
+_lib = ct.CDLL(str(_LIB_PATH))
+
+_P, _I32, _I64, _F, _SZ = ct.c_void_p, ct.c_int32, ct.c_int64, ct.c_float, ct.c_size_t
+
+
+def _sig(name, args, res=ct.c_int):
+    fn = getattr(_lib, name)
+    fn.argtypes = args
+    fn.restype = res
+    return fn
+
+
+_last_error = _sig("pkv_last_error_string", [], ct.c_char_p)
+_version = _sig("pkv_version", [])
+_read_err = _sig("pkv_read_device_error", [_P, ct.c_int])
+_scores = _sig("pkv_eviction_scores", [_P, _P, _P, _P, _P, _I64, _I32, _F, _F, _F, _P])
+_select_ws = _sig("pkv_eviction_select_workspace_size", [_I64, _I64], _SZ)
+_select = _sig("pkv_eviction_select", [_P, _I64, _I64, _P, _P, _SZ, _P])
+_fused_ws = _sig("pkv_eviction_scores_select_workspace_size", [_I64, _I64], _SZ)
+_fused = _sig("pkv_eviction_scores_select",
+              [_P, _P, _P, _P, _P, _I64, _I32, _F, _F, _F, _I64, _P, _P, _SZ, _P])
+_local = _sig("pkv_eviction_local_candidates", [_P, _I64, _I64, _I64, _P, _P, _SZ, _P])
+_merge_ws = _sig("pkv_eviction_merge_workspace_size", [_I64, _I64], _SZ)
+_merge = _sig("pkv_eviction_merge", [_P, _I64, _I64, _P, _P, _SZ, _P])
+_quant = _sig("pkv_quantize_kv_per_block", [_P, _I32, _P, _P, _I64, _I32, _I32, _I32, _P])
+_attn_ws = _sig("pkv_quant_paged_attention_workspace_size", [_I32] * 6, _SZ)
+_attn = _sig("pkv_quant_paged_attention",
+             [_P] * 8 + [_I32] * 5 + [_I64, _I32, _F, _P, _SZ, _P])
+_wtc_ws = _sig("pkv_write_to_cache_workspace_size", [_I64, _I32], _SZ)
+_wtc = _sig("pkv_write_to_cache",
+            [_P, _P, _I32, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P, _SZ, _P])
+
+LIBRARY_PATH = str(_LIB_PATH)
+_DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise RuntimeError(_last_error().decode() or f"pagedkv_fusion error {rc}")
+
+
+def _require(cond: bool, msg: str):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _workspace(nbytes: int, device) -> tuple[torch.Tensor | None, int]:
+    if nbytes == 0:
+        return None, 0
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    return ws, ws.data_ptr()
+
+
+def version() -> int:
+    return _version()
+
+
+def read_device_error(reset: bool = True) -> int:
+    """Synchronizes the current device and returns (and by default clears)
+    the error code kernels recorded there (0 = none)."""
+    code = ct.c_int32(0)
+    rc = _read_err(ct.byref(code), 1 if reset else 0)
+    if rc not in (0, 5):
+        _check(rc)
+    return int(code.value)
+
+
+# ---------------------------------------------------------------------------
+# Reference-module functions (csrc/bindings.cpp:16-25)
+# ---------------------------------------------------------------------------
+
+def eviction_scores(recency, frequency, attn_weights, valid_mask, w_recency=0.4,
+                    w_frequency=0.3, w_attention=0.3):
+    """Fused eviction score per block; see reference.py:38-71."""
+    _require(recency.is_cuda and frequency.is_cuda and attn_weights.is_cuda and valid_mask.is_cuda,
+             "all inputs must be CUDA tensors")
+    _require(recency.dtype == torch.float32, "recency must be float32")
+    _require(frequency.dtype == torch.float32, "frequency must be float32")
+    _require(attn_weights.dim() == 2, "attn_weights must be [num_blocks, block_size]")
+    _require(attn_weights.dtype == torch.float32, "attn_weights must be float32")
+    _require(valid_mask.dtype == torch.bool, "valid_mask must be bool")
+    nb, bs = attn_weights.shape
+    _require(tuple(valid_mask.shape) == (nb, bs), "valid_mask must match attn_weights")
+    _require(recency.numel() == nb and frequency.numel() == nb,
+             "recency/frequency must have num_blocks entries")
+    rec, freq = recency.contiguous(), frequency.contiguous()
+    att, msk = attn_weights.contiguous(), valid_mask.contiguous()
+    out = torch.empty(nb, dtype=torch.float32, device=rec.device)
+    _check(_scores(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
+                   out.data_ptr(), nb, bs, w_recency, w_frequency, w_attention, _stream(rec)))
+    return out
+
+
+def quant_paged_attention(q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables, seq_lens,
+                          sm_scale):
+    """INT8 paged decode attention; see reference.py:140-173."""
+    _require(q.is_cuda, "q must be a CUDA tensor")
+    _require(all(t.is_cuda for t in (k_cache_q, k_scale, v_cache_q, v_scale, block_tables,
+                                     seq_lens)), "all inputs must be CUDA tensors")
+    _require(q.dtype == torch.float32, "q must be float32 (v1)")
+    _require(k_cache_q.dtype == torch.int8, "k_cache_q must be int8")
+    _require(v_cache_q.dtype == torch.int8, "v_cache_q must be int8")
+    _require(k_scale.dtype == torch.float32 and v_scale.dtype == torch.float32,
+             "k_scale/v_scale must be float32")
+    _require(block_tables.dtype == torch.int32, "block_tables must be int32")
+    _require(q.dim() == 3 and k_cache_q.dim() == 4 and block_tables.dim() == 2,
+             "expected q [S, H, D], caches [NB, bs, Hkv, D], block_tables [S, M]")
+    S, H, D = q.shape
+    NB, bs, Hkv, Dk = k_cache_q.shape
+    _require(Dk == D and tuple(v_cache_q.shape) == tuple(k_cache_q.shape),
+             "cache head_dim must match q")
+    _require(tuple(k_scale.shape) == (NB, Hkv) and tuple(v_scale.shape) == (NB, Hkv),
+             "scales must be [num_blocks, num_kv_heads]")
+    _require(block_tables.shape[0] == S and seq_lens.numel() == S,
+             "block_tables/seq_lens must have num_seqs rows")
+    qc, kc, ks = q.contiguous(), k_cache_q.contiguous(), k_scale.contiguous()
+    vc, vs, bt = v_cache_q.contiguous(), v_scale.contiguous(), block_tables.contiguous()
+    sl = seq_lens.to(torch.int32).contiguous()
+    out = torch.empty_like(qc)
+    M = bt.shape[1]
+    ws, wp = _workspace(_attn_ws(S, H, Hkv, D, bs, M), qc.device)
+    _check(_attn(qc.data_ptr(), kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr(),
+                 bt.data_ptr(), sl.data_ptr(), out.data_ptr(), S, H, Hkv, D, bs, NB, M,
+                 float(sm_scale), wp, 0 if ws is None else ws.numel(), _stream(qc)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Entry points added by this build
+# ---------------------------------------------------------------------------
+
+def quantize_kv_per_block(kv, out_q=None, out_scale=None):
+    """Native per-(block, head) INT8 quantization; see reference.py:88-105.
+
+    ``out_q`` / ``out_scale`` (contiguous int8 / float32 CUDA tensors of the
+    result shapes, e.g. slices of a paged cache) receive the result in place
+    when given.
+    """
+    _require(kv.is_cuda, "kv must be a CUDA tensor")
+    if kv.dim() != 4:
+        raise ValueError(f"expected 4D [nb, bs, nkv, hd], got {tuple(kv.shape)}")
+    _require(kv.dtype in _DTYPE_CODE, "kv must be float32, float16 or bfloat16")
+    x = kv.contiguous()
+    nb, bs, nkv, hd = x.shape
+    if out_q is None:
+        q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    else:
+        _require(out_q.dtype == torch.int8 and tuple(out_q.shape) == tuple(x.shape)
+                 and out_q.is_contiguous() and out_q.device == x.device,
+                 "out_q must be a contiguous int8 tensor shaped like kv")
+        q = out_q
+    if out_scale is None:
+        scale = torch.empty((nb, nkv), dtype=torch.float32, device=x.device)
+    else:
+        _require(out_scale.dtype == torch.float32 and tuple(out_scale.shape) == (nb, nkv)
+                 and out_scale.is_contiguous() and out_scale.device == x.device,
+                 "out_scale must be a contiguous float32 [num_blocks, num_kv_heads] tensor")
+        scale = out_scale
+    _check(_quant(x.data_ptr(), _DTYPE_CODE[x.dtype], q.data_ptr(), scale.data_ptr(), nb, bs,
+                  nkv, hd, _stream(x)))
+    return q, scale
+
+
+def eviction_select(scores, k: int):
+    """Indices of the k lowest scores, ascending by (score, id); int64."""
+    _require(scores.is_cuda, "scores must be a CUDA tensor")
+    _require(scores.dtype == torch.float32 and scores.dim() == 1, "scores must be float32 [n]")
+    k = int(k)
+    _require(k >= 0, "k must be non-negative")
+    s = scores.contiguous()
+    n = s.numel()
+    kk = min(k, n)
+    out = torch.empty(kk, dtype=torch.int64, device=s.device)
+    if kk == 0:
+        return out
+    ws, wp = _workspace(_select_ws(n, kk), s.device)
+    _check(_select(s.data_ptr(), n, kk, out.data_ptr(), wp, ws.numel(), _stream(s)))
+    return out
+
+
+def eviction_scores_select(recency, frequency, attn_weights, valid_mask, k: int,
+                           w_recency=0.4, w_frequency=0.3, w_attention=0.3):
+    """Scores and the k selected block ids from one call: ``(scores, idx)``."""
+    _require(recency.is_cuda and frequency.is_cuda and attn_weights.is_cuda and valid_mask.is_cuda,
+             "all inputs must be CUDA tensors")
+    _require(recency.dtype == torch.float32 and frequency.dtype == torch.float32
+             and attn_weights.dtype == torch.float32, "recency/frequency/attn must be float32")
+    _require(attn_weights.dim() == 2, "attn_weights must be [num_blocks, block_size]")
+    _require(valid_mask.dtype == torch.bool, "valid_mask must be bool")
+    k = int(k)
+    _require(k >= 0, "k must be non-negative")
+    nb, bs = attn_weights.shape
+    _require(tuple(valid_mask.shape) == (nb, bs), "valid_mask must match attn_weights")
+    rec, freq = recency.contiguous(), frequency.contiguous()
+    att, msk = attn_weights.contiguous(), valid_mask.contiguous()
+    scores = torch.empty(nb, dtype=torch.float32, device=rec.device)
+    kk = min(k, nb)
+    idx = torch.empty(kk, dtype=torch.int64, device=rec.device)
+    ws, wp = _workspace(_fused_ws(nb, kk) if kk else 0, rec.device)
+    _check(_fused(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
+                  scores.data_ptr(), nb, bs, w_recency, w_frequency, w_attention, kk,
+                  idx.data_ptr(), wp, 0 if ws is None else ws.numel(), _stream(rec)))
+    return scores, idx
+
+
+def eviction_local_candidates(scores, k: int, id_offset: int = 0):
+    """This rank's min(k, n) smallest candidate keys (uint64 bit patterns
+    in an int64 tensor): orderable(score) << 32 | (id_offset + i)."""
+    _require(scores.is_cuda and scores.dtype == torch.float32, "scores must be CUDA float32")
+    s = scores.contiguous()
+    n = s.numel()
+    kk = min(int(k), n)
+    out = torch.empty(kk, dtype=torch.int64, device=s.device)
+    if kk == 0:
+        return out
+    ws, wp = _workspace(_select_ws(n, kk), s.device)
+    _check(_local(s.data_ptr(), n, kk, int(id_offset), out.data_ptr(), wp, ws.numel(),
+                  _stream(s)))
+    return out
+
+
+def eviction_merge(keys, k: int):
+    """Block ids of the k smallest gathered candidate keys, ascending."""
+    _require(keys.is_cuda and keys.dtype == torch.int64, "keys must be a CUDA int64 tensor")
+    c = keys.contiguous()
+    n = c.numel()
+    kk = min(int(k), n)
+    out = torch.empty(kk, dtype=torch.int64, device=c.device)
+    if kk == 0:
+        return out
+    ws, wp = _workspace(_merge_ws(n, kk), c.device)
+    _check(_merge(c.data_ptr(), n, kk, out.data_ptr(), wp, ws.numel(), _stream(c)))
+    return out
+
+
+def write_to_cache(key, value, kv_cache_int8, scale_cache, slot_mapping, block_size: int):
+    """Quantize + scatter new tokens into the [2, NB, bs, Hkv, D] cache
+    (integration/vllm/pagedkv_fusion_backend.py:63-95 semantics)."""
+    _require(all(t.is_cuda for t in (key, value, kv_cache_int8, scale_cache, slot_mapping)),
+             "all inputs must be CUDA tensors")
+    _require(key.dtype in _DTYPE_CODE and value.dtype == key.dtype,
+             "key/value must share a float32/float16/bfloat16 dtype")
+    _require(kv_cache_int8.dtype == torch.int8 and kv_cache_int8.dim() == 5
+             and kv_cache_int8.shape[0] == 2, "kv_cache_int8 must be int8 [2, NB, bs, Hkv, D]")
+    _require(kv_cache_int8.is_contiguous() and scale_cache.is_contiguous(),
+             "caches must be contiguous (they are written in place)")
+    _, NB, bs, Hkv, D = kv_cache_int8.shape
+    _require(int(block_size) == bs, "block_size must match the cache")
+    _require(scale_cache.dtype == torch.float32 and tuple(scale_cache.shape) == (2, NB, Hkv),
+             "scale_cache must be float32 [2, NB, Hkv]")
+    kc, vc = key.contiguous(), value.contiguous()
+    _require(tuple(kc.shape[1:]) == (Hkv, D) and kc.shape == vc.shape,
+             "key/value must be [num_tokens, Hkv, D]")
+    sm = slot_mapping.to(torch.int64).contiguous()
+    nt = kc.shape[0]
+    ws, wp = _workspace(_wtc_ws(nt, Hkv), kc.device)
+    _check(_wtc(kc.data_ptr(), vc.data_ptr(), _DTYPE_CODE[kc.dtype], kv_cache_int8.data_ptr(),
+                scale_cache.data_ptr(), sm.data_ptr(), nt, NB, bs, Hkv, D, wp,
+                0 if ws is None else ws.numel(), _stream(kc)))

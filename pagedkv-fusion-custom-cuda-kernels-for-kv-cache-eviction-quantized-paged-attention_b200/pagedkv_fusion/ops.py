@@ -1,0 +1,150 @@
+"""Public operator API -- same entry points as the reference's
+``pagedkv_fusion/ops.py`` (ops.py:40-141), with one execution path.
+
+The reference dispatches to its CUDA extension when every input is a CUDA
+tensor and otherwise falls back to NumPy.  Here every call runs the sm_100a
+kernels of ``libpagedkv_sm100.so``:
+
+* CUDA tensors are used in place (outputs stay on the device, work is
+  enqueued on the current stream, nothing synchronizes);
+* host inputs (NumPy arrays or CPU tensors) are copied to the current CUDA
+  device, processed there, and the result is returned in the caller's
+  container type after one device-to-host copy -- the same return types as
+  the reference's fallback, without a CPU implementation behind them.
+
+There is no CPU fallback: without the library or without a CUDA device the
+call raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import numpy as np
+import torch
+
+try:
+    from pagedkv_fusion import _C  # type: ignore[attr-defined]
+    _IMPORT_ERROR: Exception | None = None
+except ImportError as exc:  # pragma: no cover - exercised only without a build
+    _C = None
+    _IMPORT_ERROR = exc
+
+__all__ = [
+    "backend_in_use",
+    "eviction_scores",
+    "select_eviction_candidates",
+    "eviction_scores_and_candidates",
+    "quant_paged_attention",
+]
+
+
+def backend_in_use() -> str:
+    """'cuda' when the native library is loaded (reference ops.py:40-42)."""
+    return "cuda" if _C is not None else "unavailable"
+
+
+def _lib():
+    if _C is None:
+        raise RuntimeError(f"pagedkv_fusion native library unavailable: {_IMPORT_ERROR}")
+    if not torch.cuda.is_available():
+        raise RuntimeError("pagedkv_fusion requires a CUDA device (sm_100a); none is visible")
+    return _C
+
+
+class _Staging:
+    """Moves host inputs to the current CUDA device and results back."""
+
+    def __init__(self, *args: Any):
+        self.device = next((a.device for a in args if isinstance(a, torch.Tensor) and a.is_cuda),
+                           torch.device("cuda", torch.cuda.current_device()))
+        self.host_kind = None
+        for a in args:
+            if isinstance(a, torch.Tensor) and not a.is_cuda:
+                self.host_kind = self.host_kind or ("torch", a.device)
+            elif not isinstance(a, torch.Tensor):
+                self.host_kind = self.host_kind or ("numpy", None)
+
+    def to_device(self, a: Any, dtype: torch.dtype | None = None) -> torch.Tensor:
+        t = a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a))
+        if dtype is not None and t.dtype != dtype:
+            t = t.to(dtype)
+        if not t.is_cuda:
+            t = t.to(self.device, non_blocking=t.is_pinned())
+        return t
+
+    def back(self, t: torch.Tensor):
+        if self.host_kind is None:
+            return t
+        host = t.cpu()
+        if self.host_kind[0] == "numpy":
+            return host.numpy()
+        return host
+
+
+# ---------------------------------------------------------------------------
+# Eviction scoring and selection
+# ---------------------------------------------------------------------------
+
+def eviction_scores(recency, frequency, attn_weights, valid_mask, w_recency: float = 0.4,
+                    w_frequency: float = 0.3, w_attention: float = 0.3):
+    """Fused eviction score per KV block (lower = evict first).
+
+    Semantics of ``eviction_scores_ref`` (reference.py:38-71), bit for bit.
+    """
+    C = _lib()
+    st = _Staging(recency, frequency, attn_weights, valid_mask)
+    out = C.eviction_scores(st.to_device(recency, torch.float32),
+                            st.to_device(frequency, torch.float32),
+                            st.to_device(attn_weights, torch.float32),
+                            st.to_device(valid_mask, torch.bool),
+                            w_recency, w_frequency, w_attention)
+    return st.back(out)
+
+
+def select_eviction_candidates(scores, k: int):
+    """Indices (int64) of the k lowest-scoring blocks, ascending by score,
+    ties by lower block id (reference.py:74-81).
+
+    Unlike the reference's GPU branch (``torch.topk``, ops.py:97-98) the tie
+    order is deterministic and identical to the NumPy reference.
+    """
+    C = _lib()
+    st = _Staging(scores)
+    return st.back(C.eviction_select(st.to_device(scores, torch.float32), int(k)))
+
+
+def eviction_scores_and_candidates(recency, frequency, attn_weights, valid_mask, k: int,
+                                   w_recency: float = 0.4, w_frequency: float = 0.3,
+                                   w_attention: float = 0.3):
+    """``(scores, indices)`` from one native call: the composition
+    ``select_eviction_candidates(eviction_scores(...), k)``."""
+    C = _lib()
+    st = _Staging(recency, frequency, attn_weights, valid_mask)
+    scores, idx = C.eviction_scores_select(st.to_device(recency, torch.float32),
+                                           st.to_device(frequency, torch.float32),
+                                           st.to_device(attn_weights, torch.float32),
+                                           st.to_device(valid_mask, torch.bool), int(k),
+                                           w_recency, w_frequency, w_attention)
+    return st.back(scores), st.back(idx)
+
+
+# ---------------------------------------------------------------------------
+# Quantized paged attention
+# ---------------------------------------------------------------------------
+
+def quant_paged_attention(q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables, seq_lens,
+                          sm_scale: float):
+    """Decode-step paged attention over an INT8 paged KV cache.
+
+    Semantics of ``paged_attention_ref`` (reference.py:140-173); fp32
+    accumulation, within 1e-3 relative of the reference.
+    """
+    C = _lib()
+    st = _Staging(q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables, seq_lens)
+    out = C.quant_paged_attention(st.to_device(q, torch.float32), st.to_device(k_cache_q),
+                                  st.to_device(k_scale, torch.float32), st.to_device(v_cache_q),
+                                  st.to_device(v_scale, torch.float32),
+                                  st.to_device(block_tables, torch.int32),
+                                  st.to_device(seq_lens, torch.int32), sm_scale)
+    return st.back(out)

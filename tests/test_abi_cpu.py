@@ -1,0 +1,137 @@
+"""The C-ABI library: it loads without a GPU, exports every symbol that
+include/pagedkv_fusion.h declares, and rejects bad arguments before touching
+the device.  CPU only: no call here launches a kernel."""
+
+from __future__ import annotations
+
+import ctypes as ct
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, ensure_native_built
+
+HEADER = ROOT / "include" / "pagedkv_fusion.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(pkv_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return ct.CDLL(str(ensure_native_built()))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for required in ("pkv_eviction_scores", "pkv_eviction_select", "pkv_quant_paged_attention",
+                     "pkv_quantize_kv_per_block", "pkv_eviction_merge",
+                     "pkv_eviction_local_candidates", "pkv_write_to_cache",
+                     "pkv_last_error_string", "pkv_read_device_error"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_version_and_error_string(lib):
+    lib.pkv_version.restype = ct.c_int
+    assert lib.pkv_version() == 10000
+    lib.pkv_last_error_string.restype = ct.c_char_p
+    assert isinstance(lib.pkv_last_error_string(), bytes)
+
+
+def _err(lib):
+    lib.pkv_last_error_string.restype = ct.c_char_p
+    return lib.pkv_last_error_string().decode()
+
+
+def test_select_rejects_negative_k(lib):
+    f = lib.pkv_eviction_select
+    f.argtypes = [ct.c_void_p, ct.c_int64, ct.c_int64, ct.c_void_p, ct.c_void_p, ct.c_size_t,
+                  ct.c_void_p]
+    assert f(None, 10, -1, None, None, 0, None) == 1
+    assert "non-negative" in _err(lib)
+
+
+def test_select_with_nothing_to_do_is_ok(lib):
+    f = lib.pkv_eviction_select
+    f.argtypes = [ct.c_void_p, ct.c_int64, ct.c_int64, ct.c_void_p, ct.c_void_p, ct.c_size_t,
+                  ct.c_void_p]
+    assert f(None, 0, 5, None, None, 0, None) == 0
+
+
+def _attn(lib):
+    f = lib.pkv_quant_paged_attention
+    f.argtypes = [ct.c_void_p] * 8 + [ct.c_int32] * 5 + [ct.c_int64, ct.c_int32, ct.c_float,
+                                                          ct.c_void_p, ct.c_size_t, ct.c_void_p]
+    return f
+
+
+@pytest.mark.parametrize("shape,msg", [
+    ((4, 8, 8, 48, 16, 100), "head_dim % 32 == 0"),
+    ((4, 8, 8, 288, 16, 100), "head_dim % 32 == 0"),
+    ((4, 8, 8, 128, 128, 100), "block_size <= 64"),
+    ((4, 8, 3, 128, 16, 100), "num_heads % num_kv_heads"),
+])
+def test_decode_rejects_reference_envelope_violations(lib, shape, msg):
+    S, H, Hkv, D, bs, NB = shape
+    assert _attn(lib)(*([None] * 8), S, H, Hkv, D, bs, NB, 4, 0.1, None, 0, None) == 1
+    assert msg in _err(lib)
+
+
+def test_decode_rejects_null_pointers(lib):
+    assert _attn(lib)(*([None] * 8), 2, 8, 8, 128, 16, 10, 4, 0.1, None, 0, None) == 1
+    assert "null" in _err(lib)
+
+
+def test_decode_workspace_size(lib):
+    f = lib.pkv_quant_paged_attention_workspace_size
+    f.argtypes = [ct.c_int32] * 6
+    f.restype = ct.c_size_t
+    # 64 sequences of 128 pages: split-K partials for 8 heads x 128 dims
+    ws = f(64, 8, 8, 128, 16, 128)
+    assert ws > 64 * 8 * 128 * 4
+    assert f(0, 8, 8, 128, 16, 128) == 0
+
+
+def test_quantize_rejects_bad_dtype(lib):
+    f = lib.pkv_quantize_kv_per_block
+    f.argtypes = [ct.c_void_p, ct.c_int32, ct.c_void_p, ct.c_void_p, ct.c_int64, ct.c_int32,
+                  ct.c_int32, ct.c_int32, ct.c_void_p]
+    assert f(None, 7, None, None, 4, 16, 8, 128, None) == 1
+    assert "float32" in _err(lib)
+
+
+def test_select_workspace_is_padded_key_array(lib):
+    f = lib.pkv_eviction_select_workspace_size
+    f.argtypes = [ct.c_int64, ct.c_int64]
+    f.restype = ct.c_size_t
+    assert f(16384, 2458) == 16384 * 8
+    assert f(16385, 1) == 32768 * 8
+
+
+def test_shim_imports_and_rejects_host_tensors():
+    torch = pytest.importorskip("torch")
+    from pagedkv_fusion import _C
+    x = torch.zeros(4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.eviction_scores(x, x, torch.zeros(4, 16), torch.ones(4, 16, dtype=torch.bool))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.quant_paged_attention(torch.zeros(1, 1, 32), *([x] * 6), 0.1)
+
+
+def test_ops_fails_loudly_without_a_device():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a device is visible")
+    from pagedkv_fusion import ops
+    assert ops.backend_in_use() == "cuda"
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        ops.eviction_scores(np.zeros(2, np.float32), np.zeros(2, np.float32),
+                            np.zeros((2, 16), np.float32), np.ones((2, 16), bool))

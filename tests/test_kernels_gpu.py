@@ -1,0 +1,379 @@
+"""CUDA kernels against the oracle on the same seeded inputs.
+
+Restates the reference's GPU gate (tests/test_kernels_gpu.py: same shapes,
+rtol/atol 2e-4 for attention) and adds the stricter contract of this build:
+
+* eviction scores and int8 codes / scales bit-exact (compared as bits);
+* eviction indices equal to the oracle's, order included, with forced ties,
+  NaN / -0.0 / inf, every k from 0 to beyond n;
+* attention within 1e-3 of max|ref| (max relative error) and within the
+  reference's elementwise rtol/atol 2e-4, on both kernel paths;
+* bitwise determinism across runs.
+
+Every test calls through pagedkv_fusion._C / ops, i.e. the C ABI of
+libpagedkv_sm100.so.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, sha
+from oracle import c_oracle
+from oracle import oracle as O
+from pagedkv_fusion import problems
+
+pytestmark = pytest.mark.gpu
+
+ATTN_RTOL = 2e-4   # reference gate, tests/test_kernels_gpu.py:84
+ATTN_ATOL = 2e-4
+ATTN_MAXREL = 1e-3  # max |got - ref| / max |ref|
+
+
+def bits(a):
+    a = a.cpu().numpy() if isinstance(a, torch.Tensor) else a
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def assert_attention_close(got, want):
+    got = got.cpu().numpy() if isinstance(got, torch.Tensor) else got
+    np.testing.assert_allclose(got, want, rtol=ATTN_RTOL, atol=ATTN_ATOL)
+    scale = max(float(np.abs(want).max()), 1e-30)
+    assert float(np.abs(got - want).max()) / scale <= ATTN_MAXREL
+
+
+@pytest.fixture
+def rng():
+    return np.random.default_rng(42)
+
+
+# ---------------------------------------------------------------------------
+# eviction scores
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("num_blocks,block_size", [(1, 16), (64, 16), (517, 32), (2048, 16)])
+def test_eviction_scores_match_reference(cuda, rng, num_blocks, block_size):
+    from pagedkv_fusion import ops
+    recency = rng.random(num_blocks, dtype=np.float32)
+    frequency = rng.random(num_blocks, dtype=np.float32)
+    attn = rng.random((num_blocks, block_size), dtype=np.float32)
+    mask = rng.random((num_blocks, block_size)) > 0.2
+    want = O.eviction_scores(recency, frequency, attn, mask)
+    got = ops.eviction_scores(dev(recency), dev(frequency), dev(attn), dev(mask))
+    assert got.is_cuda and ops.backend_in_use() == "cuda"
+    np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-5, atol=1e-6)  # reference gate
+    np.testing.assert_array_equal(bits(got), bits(want))                      # this build
+
+
+def test_eviction_scores_golden_block_sizes(cuda):
+    ev = load_golden("eviction")
+    for bs in (1, 3, 7, 8, 9, 16, 17, 32, 33, 100, 128, 129, 200):
+        args = [dev(ev[f"bs{bs}_{n}"]) for n in ("rec", "freq", "attn", "mask")]
+        np.testing.assert_array_equal(bits(cuda.eviction_scores(*args)), bits(ev[f"bs{bs}_scores"]))
+        np.testing.assert_array_equal(bits(cuda.eviction_scores(*args, 0.7, 0.2, 0.1)),
+                                      bits(ev[f"bs{bs}_scores_w"]))
+
+
+def test_eviction_fully_invalid_blocks(cuda):
+    mask = torch.zeros(8, 16, dtype=torch.bool, device="cuda")
+    rec, freq = torch.rand(8, device="cuda"), torch.rand(8, device="cuda")
+    got = cuda.eviction_scores(rec, freq, torch.rand(8, 16, device="cuda"), mask)
+    assert torch.isfinite(got).all()
+    want = O.eviction_scores(rec.cpu().numpy(), freq.cpu().numpy(), np.zeros((8, 16), np.float32),
+                             np.zeros((8, 16), bool))
+    np.testing.assert_array_equal(bits(got), bits(want))
+
+
+@pytest.mark.parametrize("tag,kw", [("w16k", dict(mask="all")), ("w16k_mask", dict(mask="random")),
+                                    ("w16k_ties", dict(mask="all", ties=True))])
+def test_eviction_16k_scores_and_selection(cuda, tag, kw):
+    ev = load_golden("eviction")
+    rec, freq, att, msk = problems.eviction_problem(seed=0, **kw)
+    assert sha(rec, freq, att, msk) == str(ev[f"{tag}_digest"])
+    d = [dev(rec), dev(freq), dev(att), dev(msk)]
+    scores = cuda.eviction_scores(*d)
+    np.testing.assert_array_equal(bits(scores), bits(ev[f"{tag}_scores"]))
+    for k in (1, 2458, 8192):
+        np.testing.assert_array_equal(cuda.eviction_select(scores, k).cpu().numpy(),
+                                      ev[f"{tag}_idx_k{k}"])
+        s2, idx = cuda.eviction_scores_select(*d, k)
+        np.testing.assert_array_equal(bits(s2), bits(ev[f"{tag}_scores"]))
+        np.testing.assert_array_equal(idx.cpu().numpy(), ev[f"{tag}_idx_k{k}"])
+
+
+# ---------------------------------------------------------------------------
+# selection
+# ---------------------------------------------------------------------------
+
+def test_select_known_answers(cuda):
+    ev = load_golden("eviction")
+    np.testing.assert_array_equal(cuda.eviction_select(dev(ev["kat_scores"]), 3).cpu().numpy(),
+                                  [1, 2, 3])
+    sp = dev(ev["special_scores"])
+    np.testing.assert_array_equal(cuda.eviction_select(sp, sp.numel()).cpu().numpy(),
+                                  ev["special_idx"])
+    np.testing.assert_array_equal(cuda.eviction_select(sp, 5).cpu().numpy(), ev["special_idx_k5"])
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 100, 2047, 2048, 2049, 4096, 4097, 16384, 70001])
+def test_select_sizes_with_ties(cuda, n):
+    r = np.random.default_rng(n)
+    s = (np.floor(r.random(n) * 37) / 37).astype(np.float32)  # many exact ties
+    s[r.random(n) < 0.01] = -0.0
+    for k in sorted({0, 1, n // 7, n // 2, n, n + 5}):
+        got = cuda.eviction_select(dev(s), k).cpu().numpy()
+        np.testing.assert_array_equal(got, O.select_eviction_candidates(s, k))
+
+
+def test_select_rejects_negative_k(cuda):
+    with pytest.raises(RuntimeError, match="non-negative"):
+        cuda.eviction_select(torch.zeros(4, device="cuda"), -1)
+
+
+def test_sharded_candidates_merge_to_global_selection(cuda):
+    ev = load_golden("eviction")
+    s = ev["w16k_ties_scores"]
+    k = 2458
+    bounds = [0, 4096, 4097, 9000, 16384]
+    keys = [cuda.eviction_local_candidates(dev(s[lo:hi]), k, lo)
+            for lo, hi in zip(bounds[:-1], bounds[1:])]
+    want_keys = [O.pack_candidate_keys(s[lo:hi], np.arange(lo, hi))
+                 for lo, hi in zip(bounds[:-1], bounds[1:])]
+    for got, want in zip(keys, want_keys):
+        np.testing.assert_array_equal(got.cpu().numpy().view(np.uint64), np.sort(want)[:k])
+    merged = cuda.eviction_merge(torch.cat(keys), k).cpu().numpy()
+    np.testing.assert_array_equal(merged, ev["w16k_ties_idx_k2458"])
+
+
+# ---------------------------------------------------------------------------
+# quantization
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("case", ["rand", "edge", "tie", "f16"])
+def test_quantize_golden_bit_exact(cuda, case):
+    qz = load_golden("quantize")
+    q, s = cuda.quantize_kv_per_block(dev(qz[f"{case}_kv"]))
+    np.testing.assert_array_equal(q.cpu().numpy(), qz[f"{case}_q"])
+    np.testing.assert_array_equal(bits(s), bits(qz[f"{case}_scale"]))
+
+
+@pytest.mark.parametrize("shape", [(1, 16, 1, 32), (7, 16, 8, 128), (3, 32, 40, 128),
+                                   (5, 16, 3, 100), (2, 8, 2, 3), (257, 16, 8, 128)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_quantize_shapes_and_dtypes(cuda, shape, dtype):
+    g = torch.Generator().manual_seed(sum(shape))
+    kv = (torch.randn(shape, generator=g) * 4).to(dtype)
+    q, s = cuda.quantize_kv_per_block(kv.cuda())
+    wq, ws = O.quantize_kv_per_block(kv.float().numpy())
+    np.testing.assert_array_equal(q.cpu().numpy(), wq)
+    np.testing.assert_array_equal(bits(s), bits(ws))
+
+
+def test_quantize_heavy_tail_workload_sample(cuda):
+    # the 8,192-block heavy-tailed cache: codes of a sample of blocks
+    q, k, v, bt, sl, sm = problems.decode_heavy_tail_problem(0)
+    qk, sk = cuda.quantize_kv_per_block(dev(k))
+    idx = np.random.default_rng(3).choice(k.shape[0], 64, replace=False)
+    wq, ws = O.quantize_kv_per_block(k[idx])
+    np.testing.assert_array_equal(qk.cpu().numpy()[idx], wq)
+    np.testing.assert_array_equal(bits(sk.cpu().numpy()[idx]), bits(ws))
+    # property at full size: every code is the nearest level of its scale
+    err = (k - qk.cpu().numpy().astype(np.float32) * sk.cpu().numpy()[:, None, :, None])
+    assert (np.abs(err) <= sk.cpu().numpy()[:, None, :, None] * 0.5000001).all()
+
+
+def test_quantize_module_mirror(cuda):
+    from pagedkv_fusion.quantize import dequantize_kv_per_block, quantize_kv_per_block
+    kv = torch.randn(6, 16, 4, 64)
+    q, s = quantize_kv_per_block(kv)        # host tensor in, host tensor out
+    assert q.device.type == "cpu"
+    wq, ws = O.quantize_kv_per_block(kv.numpy())
+    np.testing.assert_array_equal(q.numpy(), wq)
+    np.testing.assert_allclose(dequantize_kv_per_block(q, s).numpy(),
+                               O.dequantize_kv_per_block(wq, ws), rtol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# paged attention
+# ---------------------------------------------------------------------------
+
+def quantized_problem(q, k, v, bt, sl, sm):
+    kq, ks = O.quantize_kv_per_block(k)
+    vq, vs = O.quantize_kv_per_block(v)
+    return q, kq, ks, vq, vs, bt, sl, sm
+
+
+def run_attention(args):
+    from pagedkv_fusion import ops
+    q, kq, ks, vq, vs, bt, sl, sm = args
+    return ops.quant_paged_attention(dev(q), dev(kq), dev(ks), dev(vq), dev(vs), dev(bt), dev(sl),
+                                     sm)
+
+
+@pytest.mark.parametrize("i", [0, 1, 2, 3])
+def test_attention_reference_shapes(cuda, i):
+    """The reference gate's four shapes, against the reference's own output."""
+    at = load_golden("attention")
+    S, H, Hkv, D, bs, L = (int(x) for x in at[f"gpu{i}_shape"])
+    prob = problems.make_paged_kv_problem(np.random.default_rng(42), S, H, Hkv, D, bs, L)
+    args = quantized_problem(*prob)
+    got = run_attention(args)
+    assert_attention_close(got, at[f"gpu{i}_out"])
+    assert_attention_close(got, c_oracle.paged_attention(*args))
+
+
+CASES = [
+    # (S, H, Hkv, D, bs, max_len, kv_scale)  -- fast path shapes
+    (4, 8, 8, 128, 16, 600, 1.0),
+    (5, 32, 8, 128, 16, 700, 1.0),    # G=4
+    (3, 16, 2, 128, 16, 1500, 1.0),   # G=8, HG=2
+    (2, 8, 1, 128, 16, 900, 1.0),     # HG=1, G=8
+    (3, 4, 4, 128, 32, 2000, 1.0),    # bs 32
+    (6, 40, 40, 128, 16, 1200, 1.0),  # 40 heads (5 groups of 8)
+    (4, 24, 12, 128, 16, 777, 3.0),   # G=2, HG=4 of 12
+    (3, 6, 6, 128, 16, 300, 0.01),    # tiny values
+    # generic path shapes
+    (4, 8, 8, 64, 16, 200, 1.0),
+    (3, 8, 2, 96, 8, 333, 1.0),
+    (2, 4, 4, 256, 16, 700, 1.0),
+    (2, 6, 3, 128, 64, 300, 1.0),
+    (2, 6, 2, 32, 24, 100, 1.0),      # group 3 (not a power of two)
+]
+
+
+@pytest.mark.parametrize("S,H,Hkv,D,bs,L,scale", CASES)
+def test_attention_cases(cuda, S, H, Hkv, D, bs, L, scale):
+    prob = problems.make_paged_kv_problem(np.random.default_rng(S * 1000 + H + D + bs), S, H,
+                                          Hkv, D, bs, L, kv_scale=scale)
+    args = quantized_problem(*prob)
+    assert_attention_close(run_attention(args), c_oracle.paged_attention(*args))
+
+
+def test_attention_forced_generic_path_agrees(cuda, monkeypatch):
+    prob = problems.make_paged_kv_problem(np.random.default_rng(9), 4, 8, 8, 128, 16, 900)
+    args = quantized_problem(*prob)
+    fast = run_attention(args)
+    monkeypatch.setenv("PKV_DECODE_GENERIC", "1")
+    slow = run_attention(args)
+    want = c_oracle.paged_attention(*args)
+    assert_attention_close(fast, want)
+    assert_attention_close(slow, want)
+
+
+@pytest.mark.parametrize("pages", ["1", "2", "8", "32"])
+def test_attention_split_sizes(cuda, monkeypatch, pages):
+    monkeypatch.setenv("PKV_DECODE_SPLIT_PAGES", pages)
+    prob = problems.make_paged_kv_problem(np.random.default_rng(11), 5, 8, 8, 128, 16, 1100)
+    args = quantized_problem(*prob)
+    assert_attention_close(run_attention(args), c_oracle.paged_attention(*args))
+
+
+def test_attention_edge_lengths(cuda):
+    at = load_golden("attention")
+    for L in (1, 15, 16, 17):
+        rng = np.random.default_rng(int(at[f"edge{L}_seed"]))
+        q, k, v, bt, sl, sm = problems.make_paged_kv_problem(rng, 1, 8, 4, 64, 16, L)
+        sl[:] = L
+        got = run_attention(quantized_problem(q, k, v, bt, sl, sm))
+        assert_attention_close(got, at[f"edge{L}_out"])
+    # fast path around page and split boundaries
+    for L in (1, 15, 16, 17, 511, 512, 513, 4096):
+        q, k, v, bt, sl, sm = problems.make_paged_kv_problem(np.random.default_rng(L), 2, 8, 8,
+                                                             128, 16, L)
+        sl[:] = L
+        args = quantized_problem(q, k, v, bt, sl, sm)
+        assert_attention_close(run_attention(args), c_oracle.paged_attention(*args))
+
+
+def test_attention_zero_length_sequence_gives_zeros(cuda):
+    q, k, v, bt, sl, sm = problems.make_paged_kv_problem(np.random.default_rng(5), 3, 8, 8, 128,
+                                                         16, 300)
+    sl[1] = 0
+    args = quantized_problem(q, k, v, bt, sl, sm)
+    got = run_attention(args).cpu().numpy()
+    assert (got[1] == 0).all()
+    assert_attention_close(got, O.paged_attention(*args))
+
+
+def test_attention_small_decode_workload(cuda):
+    at = load_golden("attention")
+    prob = problems.decode_small_problem(0)
+    args = quantized_problem(*prob)
+    assert_attention_close(run_attention(args), at["small_out"])
+
+
+def test_attention_host_inputs_roundtrip(cuda):
+    from pagedkv_fusion import ops
+    at = load_golden("attention")
+    args = quantized_problem(*problems.decode_small_problem(0))
+    got = ops.quant_paged_attention(*args)  # NumPy in, NumPy out, computed on the GPU
+    assert isinstance(got, np.ndarray)
+    assert_attention_close(got, at["small_out"])
+
+
+def test_attention_deterministic(cuda):
+    args = quantized_problem(*problems.make_paged_kv_problem(np.random.default_rng(42)))
+    a, b = run_attention(args), run_attention(args)
+    assert torch.equal(a, b)
+    args = quantized_problem(*problems.decode_small_problem(0))
+    assert torch.equal(run_attention(args), run_attention(args))
+
+
+def test_attention_bad_block_id_is_reported(cuda):
+    q, k, v, bt, sl, sm = problems.make_paged_kv_problem(np.random.default_rng(8), 2, 8, 8, 128,
+                                                         16, 64)
+    sl[:] = 64
+    bt = np.full((2, 4), 0, np.int32)
+    bt[1, 2] = 10_000_000  # far outside the cache
+    args = quantized_problem(q, k, v, bt, sl, sm)
+    cuda.read_device_error(reset=True)
+    got = run_attention(args)
+    torch.cuda.synchronize()
+    assert cuda.read_device_error(reset=True) == 1
+    assert torch.isfinite(got).all()
+    assert cuda.read_device_error(reset=True) == 0
+
+
+def test_attention_heavy_tail_workload_sample(cuda):
+    """The 64 x 2048 heavy-tailed workload at full size on the GPU, checked
+    against the double-precision oracle on 8 of its sequences."""
+    q, k, v, bt, sl, sm = problems.decode_heavy_tail_problem(0)
+    kq_d, ks_d = cuda.quantize_kv_per_block(dev(k))
+    vq_d, vs_d = cuda.quantize_kv_per_block(dev(v))
+    from pagedkv_fusion import ops
+    got = ops.quant_paged_attention(dev(q), kq_d, ks_d, vq_d, vs_d, dev(bt), dev(sl), sm)
+    pick = np.arange(0, 64, 8)
+    sub_bt = bt[pick]
+    used = np.unique(sub_bt)
+    remap = np.full(bt.max() + 1, -1, np.int64)
+    remap[used] = np.arange(used.size)
+    kq, ks = kq_d.cpu().numpy()[used], ks_d.cpu().numpy()[used]
+    vq, vs = vq_d.cpu().numpy()[used], vs_d.cpu().numpy()[used]
+    want = c_oracle.paged_attention(q[pick], kq, ks, vq, vs, remap[sub_bt].astype(np.int32),
+                                    sl[pick], sm)
+    assert_attention_close(got.cpu().numpy()[pick], want)
+    assert math.isclose(sm, 1 / math.sqrt(128))
+
+
+def test_write_to_cache_matches_oracle(cuda):
+    r = np.random.default_rng(77)
+    nb, bs, hkv, hd = 12, 16, 4, 128
+    cache = r.integers(-127, 128, (2, nb, bs, hkv, hd)).astype(np.int8)
+    scales = r.random((2, nb, hkv)).astype(np.float32)
+    key = r.standard_normal((9, hkv, hd)).astype(np.float32)
+    val = r.standard_normal((9, hkv, hd)).astype(np.float32)
+    slots = np.array([5, 6, 33, 100, 101, 102, 150, 7, 191])
+    want_c, want_s = cache.copy(), scales.copy()
+    O.write_to_cache(key, val, want_c, want_s, slots, bs)
+    dc, ds = dev(cache), dev(scales)
+    cuda.write_to_cache(dev(key), dev(val), dc, ds, dev(slots), bs)
+    np.testing.assert_array_equal(dc.cpu().numpy(), want_c)
+    np.testing.assert_array_equal(bits(ds), bits(want_s))
