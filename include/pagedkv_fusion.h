@@ -42,6 +42,7 @@ extern "C" {
 #define PKV_DEVERR_BAD_BLOCK_ID 1
 #define PKV_DEVERR_WAIT_TIMEOUT 2
 #define PKV_DEVERR_BAD_SLOT 3
+#define PKV_DEVERR_SEQ_TOO_LONG 4 /* seq_len beyond the block-table width */
 
 /* Element types of floating-point KV inputs. */
 #define PKV_DTYPE_F32 0

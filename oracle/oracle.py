@@ -210,14 +210,15 @@ def paged_attention(q, k_cache_q, k_scale, v_cache_q, v_scale,
     """Decode attention over the INT8 paged cache (reference.py:140-173).
 
     A sequence of length 0 yields zeros (the CUDA path's documented
-    behaviour; the reference raises on it).
+    behaviour; the reference raises on it).  Tokens beyond the block-table
+    width are not attended (the reference would index past the table).
     """
     q = np.asarray(q, dtype=np.float32)
     num_seqs = q.shape[0]
     bs = k_cache_q.shape[1]
     out = np.zeros(q.shape, dtype=np.float32)
     for s in range(num_seqs):
-        L = int(seq_lens[s])
+        L = min(max(int(seq_lens[s]), 0), block_tables.shape[1] * bs)
         if L == 0:
             continue
         n = (L + bs - 1) // bs

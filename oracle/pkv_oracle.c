@@ -131,7 +131,10 @@ int64_t pkv_oracle_paged_attention(const float *q, const int8_t *kq, const float
                                    int64_t max_blocks, double sm_scale) {
   const int64_t group = num_heads / num_kv_heads;
   for (int64_t s = 0; s < num_seqs; ++s) {
-    const int64_t L = seq_lens[s];
+    /* tokens beyond the block-table width are not attended (the CUDA path
+     * clamps the same way and records PKV_DEVERR_SEQ_TOO_LONG) */
+    int64_t L = seq_lens[s] > 0 ? seq_lens[s] : 0;
+    if (L > max_blocks * block_size) L = max_blocks * block_size;
     double *logit = (double *)malloc(sizeof(double) * (size_t)(L > 0 ? L : 1));
     for (int64_t h = 0; h < num_heads; ++h) {
       const int64_t kvh = h / group;

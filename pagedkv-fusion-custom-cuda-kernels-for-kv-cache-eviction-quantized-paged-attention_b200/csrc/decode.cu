@@ -238,8 +238,11 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   const int split = blockIdx.y;
   const int j0 = blockIdx.z * HG;  // first KV head of this CTA
 
-  const int L = seq_lens[seq];
-  const int n_pages = (L + BS - 1) / BS;
+  const int L_req = seq_lens[seq];
+  const int n_pages = covered_pages(L_req, BS, max_blocks_per_seq);
+  const int L = min(max(L_req, 0), n_pages * BS);
+  if (L != max(L_req, 0) && split == 0 && blockIdx.z == 0 && threadIdx.x == 0)
+    record_error(err, kDevSeqTooLong);
   const int p0 = split * pages_per_split;
   if (p0 >= n_pages) return;  // uniform across the CTA
   const int np = min(n_pages - p0, pages_per_split);
@@ -550,8 +553,11 @@ __global__ void __launch_bounds__(kGenThreads)
   const int split = blockIdx.y;
   const int h = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int L = seq_lens[seq];
-  const int n_pages = (L + bs - 1) / bs;
+  const int L_req = seq_lens[seq];
+  const int n_pages = covered_pages(L_req, bs, max_blocks_per_seq);
+  const int L = min(max(L_req, 0), n_pages * bs);
+  if (L != max(L_req, 0) && split == 0 && h == 0 && threadIdx.x == 0)
+    record_error(err, kDevSeqTooLong);
   const int p0 = split * pages_per_split;
   if (p0 >= n_pages) return;
   const int np = min(n_pages - p0, pages_per_split);
@@ -633,12 +639,11 @@ __global__ void __launch_bounds__(kGenThreads)
 __global__ void __launch_bounds__(128)
     decode_combine_kernel(const int32_t* __restrict__ seq_lens, const float* __restrict__ ws_acc,
                           const float2* __restrict__ ws_ml, float* __restrict__ out,
-                          int num_heads, int head_dim, int bs, int pages_per_split,
-                          int max_splits) {
+                          int num_heads, int head_dim, int bs, int max_blocks_per_seq,
+                          int pages_per_split, int max_splits) {
   const int seq = blockIdx.x;
   const int h = blockIdx.y;
-  const int L = seq_lens[seq];
-  const int n_pages = (L + bs - 1) / bs;
+  const int n_pages = covered_pages(seq_lens[seq], bs, max_blocks_per_seq);
   const int n_splits = (n_pages + pages_per_split - 1) / pages_per_split;
   float* o = out + ((int64_t)seq * num_heads + h) * head_dim;
   if (n_splits == 0) {
@@ -822,8 +827,8 @@ int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
   // Splits > 1 and empty sequences are finished by the combine.
   dim3 cgrid(a.num_seqs, a.num_heads);
   decode_combine_kernel<<<cgrid, 128, 0, stream>>>(a.seq_lens, ws_acc, ws_ml, a.out, a.num_heads,
-                                                   a.head_dim, a.block_size, p.pages_per_split,
-                                                   p.max_splits);
+                                                   a.head_dim, a.block_size, a.max_blocks_per_seq,
+                                                   p.pages_per_split, p.max_splits);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string("combine launch failed: ") + cudaGetErrorString(e));

@@ -26,7 +26,16 @@ enum DeviceError : int {
   kDevBadBlockId = 1,     // block table entry outside [0, num_blocks)
   kDevWaitTimeout = 2,    // a bounded barrier wait gave up
   kDevBadSlot = 3,        // slot_mapping entry outside the cache
+  kDevSeqTooLong = 4,     // seq_len needs more pages than the block table has
 };
+
+// Pages a decode split may read for a sequence: ceil(L / bs), clamped to the
+// block-table width (a longer seq_len is recorded as kDevSeqTooLong and only
+// the covered tokens are attended).  Negative lengths count as 0.
+__device__ __forceinline__ int covered_pages(int L, int bs, int max_blocks_per_seq) {
+  const int want = L > 0 ? (L + bs - 1) / bs : 0;
+  return want < max_blocks_per_seq ? want : max_blocks_per_seq;
+}
 
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
