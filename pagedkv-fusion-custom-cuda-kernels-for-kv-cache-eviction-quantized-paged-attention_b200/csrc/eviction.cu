@@ -18,98 +18,15 @@
 // merge steps between shared-memory passes.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <string>
 
+#include "eviction_score.cuh"
 #include "pkv_common.cuh"
 #include "pkv_internal.h"
 
 namespace pkv {
 namespace {
-
-// ---------------------------------------------------------------------------
-// Score
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ float masked(const float* a, const uint8_t* m, int64_t i) {
-  return m[i] ? a[i] : 0.0f;
-}
-
-// NumPy's pairwise float32 sum (see file header), on masked values.
-__device__ float pairwise_masked_sum(const float* a, const uint8_t* m, int64_t n) {
-  if (n < 8) {
-    float r = 0.0f;
-    for (int64_t i = 0; i < n; ++i) r = __fadd_rn(r, masked(a, m, i));
-    return r;
-  }
-  if (n <= 128) {
-    float r[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] = masked(a, m, j);
-    int64_t i = 8;
-    const int64_t stop = n - (n % 8);
-    for (; i < stop; i += 8) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], masked(a, m, i + j));
-    }
-    float res = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
-                          __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
-    for (; i < n; ++i) res = __fadd_rn(res, masked(a, m, i));
-    return res;
-  }
-  // n > 128: split as NumPy does (first half rounded down to a multiple of
-  // 8) and recurse, iteratively over the right spine to bound the stack.
-  int64_t half = n / 2;
-  half -= half % 8;
-  return __fadd_rn(pairwise_masked_sum(a, m, half),
-                   pairwise_masked_sum(a + half, m + half, n - half));
-}
-
-__device__ __forceinline__ float blend(float rec, float freq, float mean, float wr, float wf,
-                                       float wa) {
-  return __fadd_rn(__fadd_rn(__fmul_rn(wr, rec), __fmul_rn(wf, freq)), __fmul_rn(wa, mean));
-}
-
-// block_size 16: one thread per block, 4 x 16-byte attention loads and one
-// 16-byte mask load.
-__device__ __forceinline__ float score16(const float* attn, const uint8_t* valid, int64_t b,
-                                         float rec, float freq, float wr, float wf, float wa) {
-  const float4* ap = reinterpret_cast<const float4*>(attn + b * 16);
-  const float4 x0 = ap[0], x1 = ap[1], x2 = ap[2], x3 = ap[3];
-  const uint4 mw = *reinterpret_cast<const uint4*>(valid + b * 16);
-  const float a[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
-                       x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-  const uint32_t mws[4] = {mw.x, mw.y, mw.z, mw.w};
-  float v[16];
-  int nv = 0;
-#pragma unroll
-  for (int t = 0; t < 16; ++t) {
-    const bool ok = ((mws[t >> 2] >> ((t & 3) * 8)) & 0xffu) != 0u;
-    v[t] = ok ? a[t] : 0.0f;
-    nv += ok;
-  }
-  float r[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(v[j], v[j + 8]);
-  // NumPy reduces into an output initialised to 0.0, so the pairwise
-  // result is added to +0.0 (only visible for an all -0.0 row).
-  const float S = __fadd_rn(
-      0.0f, __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
-                      __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7]))));
-  const float mean = nv > 0 ? __fdiv_rn(S, (float)nv) : 0.0f;
-  return blend(rec, freq, mean, wr, wf, wa);
-}
-
-__device__ __forceinline__ float score_generic(const float* attn, const uint8_t* valid,
-                                               int64_t b, int bs, float rec, float freq,
-                                               float wr, float wf, float wa) {
-  const float* a = attn + b * bs;
-  const uint8_t* m = valid + b * bs;
-  int nv = 0;
-  for (int t = 0; t < bs; ++t) nv += m[t] != 0;
-  const float S = __fadd_rn(0.0f, pairwise_masked_sum(a, m, bs));
-  const float mean = nv > 0 ? __fdiv_rn(S, (float)nv) : 0.0f;
-  return blend(rec, freq, mean, wr, wf, wa);
-}
 
 template <bool BS16>
 __global__ void __launch_bounds__(256)
@@ -223,6 +140,13 @@ __global__ void emit_kernel(const uint64_t* __restrict__ keys, int64_t k, int64_
   if (out_keys) out_keys[i] = key + (uint64_t)id_offset;
 }
 
+// PKV_EVICTION_MULTI_KERNEL=1 selects the multi-kernel sort for every size
+// (used to cross-check the two paths).
+bool force_multi_kernel() {
+  const char* v = std::getenv("PKV_EVICTION_MULTI_KERNEL");
+  return v != nullptr && v[0] == '1';
+}
+
 int64_t next_pow2(int64_t n) {
   int64_t p = 2;
   while (p < n) p <<= 1;
@@ -286,6 +210,12 @@ int launch_select(const float* scores, const uint64_t* keys_in, int64_t n, int64
                   size_t workspace_bytes, cudaStream_t stream) {
   if (k > n) k = n;
   if (k <= 0) return kOk;
+  if (scores != nullptr && keys_in == nullptr && out_keys == nullptr && id_offset == 0 &&
+      n <= cluster_select_max_blocks() && !force_multi_kernel()) {
+    const int rc = launch_cluster_select(nullptr, nullptr, nullptr, nullptr, scores, nullptr, n,
+                                         0, 0.f, 0.f, 0.f, k, out_ids, stream);
+    if (rc != kUnsupported) return rc;
+  }
   const int64_t n_pad = next_pow2(n);
   if (workspace == nullptr || workspace_bytes < (size_t)n_pad * sizeof(uint64_t)) {
     set_error("workspace too small for eviction select");
@@ -313,6 +243,12 @@ int launch_scores_select(const float* recency, const float* frequency, const flo
     return kWorkspace;
   }
   if (num_blocks == 0) return kOk;
+  if (k > 0 && num_blocks <= cluster_select_max_blocks() && !force_multi_kernel()) {
+    const int rc = launch_cluster_select(recency, frequency, attn, valid, nullptr, scores,
+                                         num_blocks, block_size, w_r, w_f, w_a, k, out_ids,
+                                         stream);
+    if (rc != kUnsupported) return rc;
+  }
   uint64_t* keys = k > 0 ? static_cast<uint64_t*>(workspace) : nullptr;
   const bool fast16 = block_size == 16 && reinterpret_cast<uintptr_t>(attn) % 16 == 0 &&
                       reinterpret_cast<uintptr_t>(valid) % 16 == 0;

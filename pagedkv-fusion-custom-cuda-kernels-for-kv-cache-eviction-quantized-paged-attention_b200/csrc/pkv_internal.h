@@ -41,6 +41,15 @@ int launch_select(const float* scores, const uint64_t* keys_in, int64_t n, int64
                   int64_t id_offset, int64_t* out_ids, uint64_t* out_keys, void* workspace,
                   size_t workspace_bytes, cudaStream_t stream);
 
+// Single-launch cluster path (eviction_cluster.cu) for n <= 16,384: scores
+// from the statistics (scores_in == nullptr) or given scores; writes the k
+// selected ids.  Returns kUnsupported without launching when it cannot run.
+int launch_cluster_select(const float* rec, const float* freq, const float* attn,
+                          const uint8_t* valid, const float* scores_in, float* scores_out,
+                          int64_t n, int bs, float wr, float wf, float wa, int64_t k,
+                          int64_t* out_ids, cudaStream_t stream);
+int cluster_select_max_blocks();
+
 size_t fused_select_workspace_size(int64_t n, int64_t k);
 int launch_scores_select(const float* recency, const float* frequency, const float* attn,
                          const uint8_t* valid, float* scores, int64_t num_blocks,

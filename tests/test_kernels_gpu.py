@@ -133,6 +133,58 @@ def test_select_sizes_with_ties(cuda, n):
         np.testing.assert_array_equal(got, O.select_eviction_candidates(s, k))
 
 
+@pytest.mark.parametrize("dist", ["equal", "two_values", "nan_heavy", "neg_zero", "spread",
+                                  "clustered"])
+@pytest.mark.parametrize("n", [1, 977, 16384])
+def test_select_adversarial_distributions_both_paths(cuda, monkeypatch, dist, n):
+    """Single-launch cluster path (n <= 16384) and the multi-kernel sort on
+    distributions that defeat key-range bucketing (all keys in one bin)."""
+    r = np.random.default_rng(n + len(dist))
+    if dist == "equal":
+        s = np.full(n, 0.25, np.float32)
+    elif dist == "two_values":
+        s = np.where(r.random(n) < 0.5, 0.1, 0.7).astype(np.float32)
+    elif dist == "nan_heavy":
+        s = r.random(n).astype(np.float32)
+        s[r.random(n) < 0.6] = np.nan
+    elif dist == "neg_zero":
+        s = np.where(r.random(n) < 0.5, -0.0, 0.0).astype(np.float32)
+    elif dist == "spread":
+        s = (r.standard_normal(n) * 1e30).astype(np.float32)
+        s[::7] = np.inf
+        s[::11] = -np.inf
+    else:
+        s = (0.5 + r.random(n) * 1e-6).astype(np.float32)
+    for k in sorted({1, max(1, n // 7), n}):
+        want = O.select_eviction_candidates(s, k)
+        np.testing.assert_array_equal(cuda.eviction_select(dev(s), k).cpu().numpy(), want)
+        monkeypatch.setenv("PKV_EVICTION_MULTI_KERNEL", "1")
+        np.testing.assert_array_equal(cuda.eviction_select(dev(s), k).cpu().numpy(), want)
+        monkeypatch.delenv("PKV_EVICTION_MULTI_KERNEL")
+
+
+def test_fused_eviction_unaligned_rows_and_odd_block_size(cuda):
+    """Rows that are not 16-byte aligned take the generic scorer."""
+    r = np.random.default_rng(5)
+    n, bs = 3000, 16
+    big = r.random((n * bs + 1), dtype=np.float32)
+    att_d = dev(big)[1:].view(n, bs)          # 4-byte offset: unaligned rows
+    att = big[1:].reshape(n, bs)
+    msk = r.random((n, bs)) > 0.3
+    rec, freq = r.random(n, dtype=np.float32), r.random(n, dtype=np.float32)
+    want_s = O.eviction_scores(rec, freq, att, msk)
+    s, idx = cuda.eviction_scores_select(dev(rec), dev(freq), att_d, dev(msk), 450)
+    np.testing.assert_array_equal(bits(s), bits(want_s))
+    np.testing.assert_array_equal(idx.cpu().numpy(), O.select_eviction_candidates(want_s, 450))
+    for bs in (7, 33):
+        att = r.random((n, bs), dtype=np.float32)
+        msk = r.random((n, bs)) > 0.3
+        want_s = O.eviction_scores(rec, freq, att, msk)
+        s, idx = cuda.eviction_scores_select(dev(rec), dev(freq), dev(att), dev(msk), 999)
+        np.testing.assert_array_equal(bits(s), bits(want_s))
+        np.testing.assert_array_equal(idx.cpu().numpy(), O.select_eviction_candidates(want_s, 999))
+
+
 def test_select_rejects_negative_k(cuda):
     with pytest.raises(RuntimeError, match="non-negative"):
         cuda.eviction_select(torch.zeros(4, device="cuda"), -1)
