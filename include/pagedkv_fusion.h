@@ -162,6 +162,31 @@ int pkv_quant_paged_attention(const float *q, const int8_t *k_cache,
                               void *stream);
 
 /*
+ * pkv_quant_paged_attention without a workspace argument, for callers that
+ * cannot allocate device memory (a plugin whose host framework hands it
+ * only input/output pointers and forbids allocation, or a serving path that
+ * must not pay cudaMalloc's implicit synchronization).  Identical results.
+ * The split-K partials live in a fixed pkv_noalloc_scratch_bytes() (32 MiB)
+ * array inside the library, held on every GPU that loads the library until
+ * exit; calls needing more are rejected with PKV_ERR_UNSUPPORTED.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture).  Calls share the array: calls overlapping on the GPU
+ * race.  No counterpart in the reference.
+ */
+size_t pkv_noalloc_scratch_bytes(void);
+int pkv_quant_paged_attention_noalloc(const float *q, const int8_t *k_cache,
+                                      const float *k_scale,
+                                      const int8_t *v_cache,
+                                      const float *v_scale,
+                                      const int32_t *block_tables,
+                                      const int32_t *seq_lens, float *out,
+                                      int32_t num_seqs, int32_t num_heads,
+                                      int32_t num_kv_heads, int32_t head_dim,
+                                      int32_t block_size, int64_t num_blocks,
+                                      int32_t max_blocks_per_seq,
+                                      float sm_scale, void *stream);
+
+/*
  * Quantize new K/V tokens and scatter them into the vLLM-shaped cache
  * kv_cache int8 [2, num_blocks, block_size, num_kv_heads, head_dim] and
  * scale_cache fp32 [2, num_blocks, num_kv_heads].  The tokens of one call
