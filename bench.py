@@ -325,6 +325,9 @@ def eviction_bench(torch, C, ops, iters: int = 200):
     dev_us = []
     for _ in range(iters):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # keep the GPU busy while the host enqueues, so the events bracket
+        # device execution only (not Python launch latency)
+        torch.cuda._sleep(100_000)
         e0.record(stream)
         C.eviction_scores_select(*d, k)
         e1.record(stream)

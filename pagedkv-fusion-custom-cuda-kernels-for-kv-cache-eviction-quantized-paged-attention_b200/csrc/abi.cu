@@ -101,7 +101,7 @@ int pkv_eviction_scores(const float* recency, const float* frequency, const floa
 }
 
 size_t pkv_eviction_select_workspace_size(int64_t num_blocks, int64_t k) {
-  return pkv::select_workspace_size(num_blocks, k);
+  return pkv::scores_select_workspace_size(num_blocks, k);
 }
 
 static int check_select(int64_t n, int64_t k, const void* in, const void* out) {

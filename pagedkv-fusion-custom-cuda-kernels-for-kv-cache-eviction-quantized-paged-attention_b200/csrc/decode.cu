@@ -147,17 +147,6 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
          ((uint32_t)(d & 255) << 24);
 }
 
-// int8 byte i of w -> float, exactly: the biased byte becomes the low
-// mantissa bits of 2^23, and the bias is subtracted in one float op.
-__device__ __forceinline__ void bytes_to_float4(uint32_t w, float& f0, float& f1, float& f2,
-                                                float& f3) {
-  const uint32_t u = w ^ 0x80808080u;
-  f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.0f;
-  f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.0f;
-  f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.0f;
-  f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.0f;
-}
-
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -178,7 +167,6 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
 
 constexpr int kFastStages = 4;
 constexpr int kStageBytes = 128 * 128;  // 128 cache lines of 128 B
-constexpr int kMaxTok = 512;            // tokens per split
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kFastThreads = kConsumers + 32;
@@ -190,15 +178,23 @@ struct FastCfg {
   static constexpr int kPPS = 128 / kLinesPerPage;  // pages per stage
   static constexpr int kPageBytes = kLinesPerPage * 128;
   static constexpr int kTokPerStage = kPPS * BS;
-  static constexpr int kMaxPages = kMaxTok / BS;
   static constexpr int kNHG = HG * G;  // query heads handled by one CTA
   static_assert(kNHG <= 16, "query heads per CTA");
-  static constexpr int kR = kConsumerWarps / HG;  // token slices in the V phase
+  static constexpr int kMaxTok = kNHG <= 8 ? 512 : 256;  // tokens per split
+  static constexpr int kMaxPages = kMaxTok / BS;
+  // p.V work units: (kv head, pair of its query heads); token slices split
+  // the 8 consumer warps between units.
+  static constexpr int kGPW = G < 2 ? G : 2;
+  static constexpr int kUnits = HG * (G / kGPW);
+  static_assert(kUnits <= kConsumerWarps && kConsumerWarps % kUnits == 0, "p.V warp map");
+  static constexpr int kVR = kConsumerWarps / kUnits;
   static constexpr int kQdStride = 3 * 128 + 16;  // padded: spreads banks
   static constexpr int kOffLogit = kFastStages * kStageBytes;
-  static constexpr int kOffQd = kOffLogit + kNHG * kMaxTok * 4;
+  static constexpr int kOffPd = kOffLogit + kNHG * kMaxTok * 4;  // [kNHG][3][kMaxTok] bytes
+  static constexpr int kOffQd = kOffPd + kNHG * 3 * kMaxTok;
   static constexpr int kOffQs = kOffQd + (G > 1 ? kNHG * kQdStride : 0);
-  static constexpr int kOffMl = kOffQs + 64;
+  static constexpr int kOffVsc = kOffQs + 64;
+  static constexpr int kOffMl = kOffVsc + 64;
   static constexpr int kOffPhys = kOffMl + 16 * 8;
   static constexpr int kOffKs = kOffPhys + kMaxPages * 4;
   static constexpr int kOffVs = kOffKs + kMaxPages * HG * 4;
@@ -206,6 +202,13 @@ struct FastCfg {
   static constexpr int kOffFlag = kOffBar + 2 * kFastStages * 8;
   static constexpr int kSmemBytes = kOffFlag + 16 + 1024;  // + alignment slack
 };
+
+// Signed int8 bytes of a times unsigned bytes of b, summed into c.
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 
 template <int BS, int HG, int G>
 __global__ void __launch_bounds__(kFastThreads, 2)
@@ -420,7 +423,7 @@ __global__ void __launch_bounds__(kFastThreads, 2)
         part += __shfl_xor_sync(0xffffffffu, part, 1);
         const float qs = (G == 1) ? my_qs : s_qs[k_jj * G + g];
         if (k_half == 0 && tok < T)
-          s_logit[(k_jj * G + g) * kMaxTok + tok] = valid ? part * (qs * ks * qk_scale) : -INFINITY;
+          s_logit[(k_jj * G + g) * C::kMaxTok + tok] = valid ? part * (qs * ks * qk_scale) : -INFINITY;
       }
     }
     __syncwarp();
@@ -429,29 +432,58 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   named_barrier(1, kConsumers);
 
   // ---- softmax over the split (per query head) ---------------------------
+  // p_t = 2^(logit_t - m).  For p.V each p_t * vs(page) is written as a
+  // 24-bit fixed-point fraction of the split's largest V scale, in three
+  // unsigned byte planes (tokens up to the next multiple of 4 included, as
+  // zeros past T).
+  uint8_t* s_pd = smem + C::kOffPd;
+  float* s_vsc = reinterpret_cast<float*>(smem + C::kOffVsc);
+  const int T4 = (T + 3) & ~3;
   for (int hg = warp; hg < C::kNHG; hg += kConsumerWarps) {
-    float* row = s_logit + hg * kMaxTok;
+    const float* row = s_logit + hg * C::kMaxTok;
     float m = -INFINITY;
     for (int t = lane; t < T; t += 32) m = fmaxf(m, row[t]);
     m = warp_max(m);
     const int jj = hg / G;
+    float vmax = 0.0f;
+    for (int pg = lane; pg < np; pg += 32) vmax = fmaxf(vmax, s_vs[pg * HG + jj]);
+    vmax = warp_max(vmax);
+    const float to_fix = vmax > 0.0f ? 16777215.0f / vmax : 0.0f;
+    uint8_t* pd = s_pd + hg * 3 * C::kMaxTok;
     float l = 0.0f;
-    for (int t = lane; t < T; t += 32) {
-      const float p = (m == -INFINITY) ? 0.0f : exp2f(row[t] - m);
-      l += p;
-      row[t] = p * s_vs[(t / BS) * HG + jj];
+    for (int t = lane; t < T4; t += 32) {
+      uint32_t n = 0;
+      if (t < T && m != -INFINITY) {
+        const float p = exp2f(row[t] - m);
+        l += p;
+        n = __float2uint_rn(fminf(p * s_vs[(t / BS) * HG + jj] * to_fix, 16777215.0f));
+      }
+      pd[t] = (uint8_t)(n & 255u);
+      pd[C::kMaxTok + t] = (uint8_t)((n >> 8) & 255u);
+      pd[2 * C::kMaxTok + t] = (uint8_t)(n >> 16);
     }
     l = warp_sum(l);
-    if (lane == 0) s_ml[hg] = make_float2(m, l);
+    if (lane == 0) {
+      s_ml[hg] = make_float2(m, l);
+      s_vsc[hg] = vmax * (1.0f / 16777215.0f);
+    }
   }
   named_barrier(1, kConsumers);
 
-  // ---- V phase -------------------------------------------------------------
-  const int v_jj = warp % HG;
-  const int v_r = warp / HG;
-  float acc[G][4];
+  // ---- V phase: integer p.V ----------------------------------------------
+  // A warp owns (kv head v_jj, query heads g0 .. g0+kGPW-1, token slice v_r);
+  // lane w owns channels 4w .. 4w+3.  Per 4 tokens: 4 V words, a 4x4 byte
+  // transpose (8 prmt) to put one channel of 4 tokens in a word, then one
+  // dp4a per (channel, digit plane, query head).
+  const int unit = warp % C::kUnits;
+  const int v_r = warp / C::kUnits;
+  const int v_jj = unit / (G / C::kGPW);
+  const int g0 = (unit % (G / C::kGPW)) * C::kGPW;
+  int iacc[C::kGPW][3][4];
 #pragma unroll
-  for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
+  for (int g = 0; g < C::kGPW; ++g)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) iacc[g][j][0] = iacc[g][j][1] = iacc[g][j][2] = iacc[g][j][3] = 0;
   const uint32_t word_off = (uint32_t)((lane & 3) << 2);
   const int chunk = lane >> 2;
   for (int st = 0; st < n_stages; ++st) {
@@ -465,42 +497,61 @@ __global__ void __launch_bounds__(kFastThreads, 2)
     if (live) {
       const uint32_t base = stage_base + slot * kStageBytes;
       const int tok0 = st * C::kTokPerStage;
-      const int tcount = min(C::kTokPerStage, T - tok0);
-#pragma unroll 4
-      for (int ts = v_r; ts < tcount; ts += C::kR) {
-        const int line = ts * HG + v_jj;
-        const uint32_t w = lds32(base + line * 128 + ((chunk ^ (line & 7)) << 4) + word_off);
-        float f0, f1, f2, f3;
-        bytes_to_float4(w, f0, f1, f2, f3);
+      const int ngroups = (min(C::kTokPerStage, T - tok0) + 3) >> 2;
+#pragma unroll 2
+      for (int gi = v_r; gi < ngroups; gi += C::kVR) {
+        const int ts = gi * 4;
+        uint32_t w[4];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float p = s_logit[(v_jj * G + g) * kMaxTok + tok0 + ts];
-          acc[g][0] = fmaf(p, f0, acc[g][0]);
-          acc[g][1] = fmaf(p, f1, acc[g][1]);
-          acc[g][2] = fmaf(p, f2, acc[g][2]);
-          acc[g][3] = fmaf(p, f3, acc[g][3]);
+        for (int u = 0; u < 4; ++u) {
+          const int line = (ts + u) * HG + v_jj;
+          w[u] = lds32(base + line * 128 + ((chunk ^ (line & 7)) << 4) + word_off);
+        }
+        const uint32_t t0 = __byte_perm(w[0], w[1], 0x5140), t1 = __byte_perm(w[0], w[1], 0x7362);
+        const uint32_t t2 = __byte_perm(w[2], w[3], 0x5140), t3 = __byte_perm(w[2], w[3], 0x7362);
+        const uint32_t c[4] = {__byte_perm(t0, t2, 0x5410), __byte_perm(t0, t2, 0x7632),
+                               __byte_perm(t1, t3, 0x5410), __byte_perm(t1, t3, 0x7632)};
+#pragma unroll
+        for (int g = 0; g < C::kGPW; ++g) {
+          const uint8_t* pd = s_pd + (v_jj * G + g0 + g) * 3 * C::kMaxTok + tok0 + ts;
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            const uint32_t pw = lds32(smem_u32(pd + j * C::kMaxTok));
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) iacc[g][j][ch] = dp4a_su(c[ch], pw, iacc[g][j][ch]);
+          }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
+  // integer planes -> fp32 (each plane sum < 2^24: exact)
+  float acc[C::kGPW][4];
+#pragma unroll
+  for (int g = 0; g < C::kGPW; ++g) {
+    const float sc = s_vsc[v_jj * G + g0 + g];
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch)
+      acc[g][ch] = sc * ((float)iacc[g][2][ch] * 65536.0f +
+                         ((float)iacc[g][1][ch] * 256.0f + (float)iacc[g][0][ch]));
+  }
 
   // ---- reduce token slices, then write -------------------------------------
-  if constexpr (C::kR > 1) {
+  if constexpr (C::kVR > 1) {
     named_barrier(1, kConsumers);  // every stage consumed: the ring is free
     float* red = reinterpret_cast<float*>(smem);
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-      reinterpret_cast<float4*>(red + ((v_r * HG + v_jj) * G + g) * 128)[lane] =
+    for (int g = 0; g < C::kGPW; ++g)
+      reinterpret_cast<float4*>(red + ((v_r * C::kUnits + unit) * C::kGPW + g) * 128)[lane] =
           make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
     named_barrier(1, kConsumers);
     if (v_r == 0) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        for (int r = 1; r < C::kR; ++r) {
-          const float4 o =
-              reinterpret_cast<const float4*>(red + ((r * HG + v_jj) * G + g) * 128)[lane];
+      for (int g = 0; g < C::kGPW; ++g) {
+        for (int r = 1; r < C::kVR; ++r) {
+          const float4 o = reinterpret_cast<const float4*>(
+              red + ((r * C::kUnits + unit) * C::kGPW + g) * 128)[lane];
           acc[g][0] += o.x;
           acc[g][1] += o.y;
           acc[g][2] += o.z;
@@ -511,9 +562,9 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   }
   if (v_r == 0) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const int hg = v_jj * G + g;
-      const int hq = (j0 + v_jj) * G + g;
+    for (int g = 0; g < C::kGPW; ++g) {
+      const int hg = v_jj * G + g0 + g;
+      const int hq = (j0 + v_jj) * G + g0 + g;
       const float2 ml = s_ml[hg];
       if (n_splits == 1) {
         const float inv = ml.y > 0.0f ? 1.0f / ml.y : 0.0f;
@@ -712,7 +763,7 @@ Plan make_plan(const DecodeArgs& a) {
   }
   if (p.fast) {
     const int pps_stage = 128 / (a.block_size * p.hg);
-    const int max_pages = kMaxTok / a.block_size;
+    const int max_pages = (p.hg * p.g <= 8 ? 512 : 256) / a.block_size;
     const int groups = a.num_kv_heads / p.hg;
     int pps = max_pages;
     const int64_t target = env_int("PKV_DECODE_TARGET_CTAS", 888);

@@ -205,6 +205,15 @@ size_t select_workspace_size(int64_t n, int64_t k) {
   return (size_t)next_pow2(n < 2 ? 2 : n) * sizeof(uint64_t);
 }
 
+// Selections of at most 16,384 scores run in one cluster launch with no
+// workspace when this device can schedule the cluster.
+static size_t select_workspace_size_for_call(int64_t n, int64_t k) {
+  if (k > 0 && n <= cluster_select_max_blocks() && !force_multi_kernel() &&
+      cluster_select_available())
+    return 0;
+  return select_workspace_size(n, k);
+}
+
 int launch_select(const float* scores, const uint64_t* keys_in, int64_t n, int64_t k,
                   int64_t id_offset, int64_t* out_ids, uint64_t* out_keys, void* workspace,
                   size_t workspace_bytes, cudaStream_t stream) {
@@ -229,7 +238,13 @@ int launch_select(const float* scores, const uint64_t* keys_in, int64_t n, int64
   return check_launch("eviction emit");
 }
 
-size_t fused_select_workspace_size(int64_t n, int64_t k) { return select_workspace_size(n, k); }
+size_t fused_select_workspace_size(int64_t n, int64_t k) {
+  return select_workspace_size_for_call(n, k);
+}
+
+size_t scores_select_workspace_size(int64_t n, int64_t k) {
+  return select_workspace_size_for_call(n, k);
+}
 
 int launch_scores_select(const float* recency, const float* frequency, const float* attn,
                          const uint8_t* valid, float* scores, int64_t num_blocks,
@@ -237,17 +252,17 @@ int launch_scores_select(const float* recency, const float* frequency, const flo
                          int64_t* out_ids, void* workspace, size_t workspace_bytes,
                          cudaStream_t stream) {
   if (k > num_blocks) k = num_blocks;
-  const int64_t n_pad = next_pow2(num_blocks < 2 ? 2 : num_blocks);
-  if (k > 0 && (workspace == nullptr || workspace_bytes < (size_t)n_pad * sizeof(uint64_t))) {
-    set_error("workspace too small for fused eviction");
-    return kWorkspace;
-  }
   if (num_blocks == 0) return kOk;
   if (k > 0 && num_blocks <= cluster_select_max_blocks() && !force_multi_kernel()) {
     const int rc = launch_cluster_select(recency, frequency, attn, valid, nullptr, scores,
                                          num_blocks, block_size, w_r, w_f, w_a, k, out_ids,
                                          stream);
     if (rc != kUnsupported) return rc;
+  }
+  const int64_t n_pad = next_pow2(num_blocks < 2 ? 2 : num_blocks);
+  if (k > 0 && (workspace == nullptr || workspace_bytes < (size_t)n_pad * sizeof(uint64_t))) {
+    set_error("workspace too small for fused eviction");
+    return kWorkspace;
   }
   uint64_t* keys = k > 0 ? static_cast<uint64_t*>(workspace) : nullptr;
   const bool fast16 = block_size == 16 && reinterpret_cast<uintptr_t>(attn) % 16 == 0 &&

@@ -303,6 +303,8 @@ int cluster_size_for_device() {
 
 int cluster_select_max_blocks() { return kMaxN; }
 
+bool cluster_select_available() { return cluster_size_for_device() != 0; }
+
 // Returns kUnsupported (without launching) when the cluster path cannot
 // run here, so the caller can use the multi-kernel path instead.
 int launch_cluster_select(const float* rec, const float* freq, const float* attn,

@@ -49,6 +49,10 @@ int launch_cluster_select(const float* rec, const float* freq, const float* attn
                           int64_t n, int bs, float wr, float wf, float wa, int64_t k,
                           int64_t* out_ids, cudaStream_t stream);
 int cluster_select_max_blocks();
+// True when the current device can schedule the selection cluster.
+bool cluster_select_available();
+// Workspace bytes for pkv_eviction_select: 0 when the cluster path runs.
+size_t scores_select_workspace_size(int64_t n, int64_t k);
 
 size_t fused_select_workspace_size(int64_t n, int64_t k);
 int launch_scores_select(const float* recency, const float* frequency, const float* attn,

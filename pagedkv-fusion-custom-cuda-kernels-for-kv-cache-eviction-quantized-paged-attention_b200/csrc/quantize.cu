@@ -119,10 +119,79 @@ __global__ void __launch_bounds__(kQThreads)
   }
 }
 
+// head_dim 128: one warp per (block, kv head).  Lane l holds channels
+// 4l .. 4l+3 of all BS tokens in registers (BS independent loads in flight),
+// so the block is read once: warp max -> scale -> codes, no shared memory.
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&f)[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&f)[4]) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+}
+template <>
+__device__ __forceinline__ void load4<__half>(const __half* p, float (&f)[4]) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+template <>
+__device__ __forceinline__ void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&f)[4]) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+
+template <typename T, int BS>
+__global__ void __launch_bounds__(kQThreads)
+    quantize_d128_kernel(const T* __restrict__ kv, int8_t* __restrict__ q,
+                         float* __restrict__ scale, int64_t units, int hkv) {
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = (int64_t)blockIdx.x * (kQThreads / 32) + (threadIdx.x >> 5);
+  if (unit >= units) return;  // whole warp
+  const int64_t b = unit / hkv;
+  const int h = (int)(unit - b * hkv);
+  const int64_t tok_stride = (int64_t)hkv * 128;
+  const int64_t base = (b * BS * hkv + h) * 128 + lane * 4;
+  float v[BS][4];
+  uint32_t m = 0u;
+#pragma unroll
+  for (int t = 0; t < BS; ++t) {
+    load4<T>(kv + base + t * tok_stride, v[t]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m = max(m, __float_as_uint(v[t][i]) & 0x7fffffffu);
+  }
+  m = __reduce_max_sync(0xffffffffu, m);  // NaN bits exceed +inf: NaN wins
+  const float amax = __uint_as_float(m);
+  const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+  if (lane == 0) scale[unit] = s;
+#pragma unroll
+  for (int t = 0; t < BS; ++t) {
+    const uint32_t w = (uint32_t)(quantize_one(v[t][0], s) & 255) |
+                       ((uint32_t)(quantize_one(v[t][1], s) & 255) << 8) |
+                       ((uint32_t)(quantize_one(v[t][2], s) & 255) << 16) |
+                       ((uint32_t)(quantize_one(v[t][3], s) & 255) << 24);
+    *reinterpret_cast<uint32_t*>(q + base + t * tok_stride) = w;
+  }
+}
+
 template <typename T>
 int launch_quantize_t(const T* kv, int8_t* q, float* scale, int64_t nb, int bs, int hkv, int hd,
                       cudaStream_t stream) {
   constexpr int VEC = 16 / sizeof(T);
+  if (hd == 128 && (bs == 16 || bs == 32) &&
+      reinterpret_cast<uintptr_t>(kv) % (4 * sizeof(T)) == 0 &&
+      reinterpret_cast<uintptr_t>(q) % 4 == 0) {
+    const int64_t units = nb * hkv;
+    const unsigned grid = (unsigned)((units + kQThreads / 32 - 1) / (kQThreads / 32));
+    if (bs == 16)
+      quantize_d128_kernel<T, 16><<<grid, kQThreads, 0, stream>>>(kv, q, scale, units, hkv);
+    else
+      quantize_d128_kernel<T, 32><<<grid, kQThreads, 0, stream>>>(kv, q, scale, units, hkv);
+    return kOk;
+  }
   const bool vec = hd % VEC == 0 && reinterpret_cast<uintptr_t>(kv) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(q) % VEC == 0;
   const size_t smem = (size_t)hkv * sizeof(uint32_t);

@@ -69,7 +69,8 @@ def _require(cond: bool, msg: str):
 
 
 def _stream(t: torch.Tensor) -> int:
-    return torch.cuda.current_stream(t.device).cuda_stream
+    """Raw cudaStream_t of the current stream on ``t``'s device."""
+    return torch._C._cuda_getCurrentRawStream(t.device.index)
 
 
 def _workspace(nbytes: int, device) -> tuple[torch.Tensor | None, int]:
@@ -202,7 +203,8 @@ def eviction_select(scores, k: int):
     if kk == 0:
         return out
     ws, wp = _workspace(_select_ws(n, kk), s.device)
-    _check(_select(s.data_ptr(), n, kk, out.data_ptr(), wp, ws.numel(), _stream(s)))
+    _check(_select(s.data_ptr(), n, kk, out.data_ptr(), wp, 0 if ws is None else ws.numel(),
+                   _stream(s)))
     return out
 
 
@@ -241,7 +243,7 @@ def eviction_local_candidates(scores, k: int, id_offset: int = 0):
     out = torch.empty(kk, dtype=torch.int64, device=s.device)
     if kk == 0:
         return out
-    ws, wp = _workspace(_select_ws(n, kk), s.device)
+    ws, wp = _workspace(_merge_ws(n, kk), s.device)
     _check(_local(s.data_ptr(), n, kk, int(id_offset), out.data_ptr(), wp, ws.numel(),
                   _stream(s)))
     return out

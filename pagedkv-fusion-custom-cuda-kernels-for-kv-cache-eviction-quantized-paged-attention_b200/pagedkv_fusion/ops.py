@@ -44,12 +44,25 @@ def backend_in_use() -> str:
     return "cuda" if _C is not None else "unavailable"
 
 
+_DEVICE_OK = False
+
+
 def _lib():
+    global _DEVICE_OK
     if _C is None:
         raise RuntimeError(f"pagedkv_fusion native library unavailable: {_IMPORT_ERROR}")
-    if not torch.cuda.is_available():
-        raise RuntimeError("pagedkv_fusion requires a CUDA device (sm_100a); none is visible")
+    if not _DEVICE_OK:
+        if not torch.cuda.is_available():
+            raise RuntimeError("pagedkv_fusion requires a CUDA device (sm_100a); none is visible")
+        _DEVICE_OK = True
     return _C
+
+
+def _all_cuda(*args) -> bool:
+    for a in args:
+        if not (isinstance(a, torch.Tensor) and a.is_cuda):
+            return False
+    return True
 
 
 class _Staging:
@@ -93,6 +106,9 @@ def eviction_scores(recency, frequency, attn_weights, valid_mask, w_recency: flo
     Semantics of ``eviction_scores_ref`` (reference.py:38-71), bit for bit.
     """
     C = _lib()
+    if _all_cuda(recency, frequency, attn_weights, valid_mask):
+        return C.eviction_scores(recency, frequency, attn_weights, valid_mask, w_recency,
+                                 w_frequency, w_attention)
     st = _Staging(recency, frequency, attn_weights, valid_mask)
     out = C.eviction_scores(st.to_device(recency, torch.float32),
                             st.to_device(frequency, torch.float32),
@@ -110,6 +126,8 @@ def select_eviction_candidates(scores, k: int):
     order is deterministic and identical to the NumPy reference.
     """
     C = _lib()
+    if _all_cuda(scores):
+        return C.eviction_select(scores, int(k))
     st = _Staging(scores)
     return st.back(C.eviction_select(st.to_device(scores, torch.float32), int(k)))
 
@@ -141,6 +159,9 @@ def quant_paged_attention(q, k_cache_q, k_scale, v_cache_q, v_scale, block_table
     accumulation, within 1e-3 relative of the reference.
     """
     C = _lib()
+    if _all_cuda(q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables, seq_lens):
+        return C.quant_paged_attention(q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables,
+                                       seq_lens, sm_scale)
     st = _Staging(q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables, seq_lens)
     out = C.quant_paged_attention(st.to_device(q, torch.float32), st.to_device(k_cache_q),
                                   st.to_device(k_scale, torch.float32), st.to_device(v_cache_q),
