@@ -333,6 +333,12 @@ def eviction_bench(torch, C, ops, iters: int = 200):
         e1.record(stream)
         e1.synchronize()
         dev_us.append(e0.elapsed_time(e1) * 1e3)
+    fused_wall = []
+    for _ in range(iters):  # one fused call + sync
+        t0 = time.perf_counter()
+        ops.eviction_scores_and_candidates(*d, k)
+        torch.cuda.synchronize()
+        fused_wall.append((time.perf_counter() - t0) * 1e6)
     wall = []
     for _ in range(iters):  # the reference's measure: two ops calls + sync
         t0 = time.perf_counter()
@@ -348,6 +354,7 @@ def eviction_bench(torch, C, ops, iters: int = 200):
     return {"config": "16384 blocks x 16 tokens, k=2458", "exact": exact,
             "device_p50_us": statistics.median(dev_us),
             "device_p90_us": statistics.quantiles(dev_us, n=10)[8],
+            "fused_wall_p50_us": statistics.median(fused_wall),
             "wall_p50_us": statistics.median(wall),
             "wall_p90_us": statistics.quantiles(wall, n=10)[8],
             "cpu_port_p50_us": statistics.median(cpu)}

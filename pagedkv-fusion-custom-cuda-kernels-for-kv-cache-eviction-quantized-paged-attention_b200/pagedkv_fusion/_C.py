@@ -98,25 +98,37 @@ def read_device_error(reset: bool = True) -> int:
 # Reference-module functions (csrc/bindings.cpp:16-25)
 # ---------------------------------------------------------------------------
 
+_F32, _BOOL = torch.float32, torch.bool
+
+
 def eviction_scores(recency, frequency, attn_weights, valid_mask, w_recency=0.4,
                     w_frequency=0.3, w_attention=0.3):
     """Fused eviction score per block; see reference.py:38-71."""
-    _require(recency.is_cuda and frequency.is_cuda and attn_weights.is_cuda and valid_mask.is_cuda,
-             "all inputs must be CUDA tensors")
-    _require(recency.dtype == torch.float32, "recency must be float32")
-    _require(frequency.dtype == torch.float32, "frequency must be float32")
-    _require(attn_weights.dim() == 2, "attn_weights must be [num_blocks, block_size]")
-    _require(attn_weights.dtype == torch.float32, "attn_weights must be float32")
-    _require(valid_mask.dtype == torch.bool, "valid_mask must be bool")
+    if not (recency.is_cuda and frequency.is_cuda and attn_weights.is_cuda
+            and valid_mask.is_cuda):
+        raise RuntimeError("all inputs must be CUDA tensors")
+    if recency.dtype is not _F32:
+        raise RuntimeError("recency must be float32")
+    if attn_weights.dim() != 2:
+        raise RuntimeError("attn_weights must be [num_blocks, block_size]")
+    if valid_mask.dtype is not _BOOL:
+        raise RuntimeError("valid_mask must be bool")
+    if frequency.dtype is not _F32 or attn_weights.dtype is not _F32:
+        raise RuntimeError("frequency and attn_weights must be float32")
     nb, bs = attn_weights.shape
-    _require(tuple(valid_mask.shape) == (nb, bs), "valid_mask must match attn_weights")
-    _require(recency.numel() == nb and frequency.numel() == nb,
-             "recency/frequency must have num_blocks entries")
-    rec, freq = recency.contiguous(), frequency.contiguous()
-    att, msk = attn_weights.contiguous(), valid_mask.contiguous()
-    out = torch.empty(nb, dtype=torch.float32, device=rec.device)
-    _check(_scores(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
-                   out.data_ptr(), nb, bs, w_recency, w_frequency, w_attention, _stream(rec)))
+    if valid_mask.shape != attn_weights.shape or recency.numel() != nb or frequency.numel() != nb:
+        raise RuntimeError("valid_mask must match attn_weights; recency/frequency need "
+                           "num_blocks entries")
+    rec = recency if recency.is_contiguous() else recency.contiguous()
+    freq = frequency if frequency.is_contiguous() else frequency.contiguous()
+    att = attn_weights if attn_weights.is_contiguous() else attn_weights.contiguous()
+    msk = valid_mask if valid_mask.is_contiguous() else valid_mask.contiguous()
+    out = torch.empty(nb, dtype=_F32, device=rec.device)
+    rc = _scores(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
+                 out.data_ptr(), nb, bs, w_recency, w_frequency, w_attention,
+                 torch._C._cuda_getCurrentRawStream(rec.device.index))
+    if rc:
+        _check(rc)
     return out
 
 
@@ -192,19 +204,25 @@ def quantize_kv_per_block(kv, out_q=None, out_scale=None):
 
 def eviction_select(scores, k: int):
     """Indices of the k lowest scores, ascending by (score, id); int64."""
-    _require(scores.is_cuda, "scores must be a CUDA tensor")
-    _require(scores.dtype == torch.float32 and scores.dim() == 1, "scores must be float32 [n]")
+    if not scores.is_cuda:
+        raise RuntimeError("scores must be a CUDA tensor")
+    if scores.dtype is not _F32 or scores.dim() != 1:
+        raise RuntimeError("scores must be float32 [n]")
     k = int(k)
-    _require(k >= 0, "k must be non-negative")
-    s = scores.contiguous()
+    if k < 0:
+        raise RuntimeError("k must be non-negative")
+    s = scores if scores.is_contiguous() else scores.contiguous()
     n = s.numel()
-    kk = min(k, n)
+    kk = k if k < n else n
     out = torch.empty(kk, dtype=torch.int64, device=s.device)
     if kk == 0:
         return out
-    ws, wp = _workspace(_select_ws(n, kk), s.device)
-    _check(_select(s.data_ptr(), n, kk, out.data_ptr(), wp, 0 if ws is None else ws.numel(),
-                   _stream(s)))
+    nbytes = _select_ws(n, kk)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=s.device) if nbytes else None
+    rc = _select(s.data_ptr(), n, kk, out.data_ptr(), 0 if ws is None else ws.data_ptr(),
+                 nbytes, torch._C._cuda_getCurrentRawStream(s.device.index))
+    if rc:
+        _check(rc)
     return out
 
 

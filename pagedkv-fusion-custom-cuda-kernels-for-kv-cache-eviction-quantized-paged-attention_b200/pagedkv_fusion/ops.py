@@ -89,7 +89,10 @@ class _Staging:
     def back(self, t: torch.Tensor):
         if self.host_kind is None:
             return t
-        host = t.cpu()
+        # pinned destination, asynchronous copy, then wait on this stream only
+        host = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        host.copy_(t, non_blocking=True)
+        torch.cuda.current_stream(t.device).synchronize()
         if self.host_kind[0] == "numpy":
             return host.numpy()
         return host
@@ -138,6 +141,9 @@ def eviction_scores_and_candidates(recency, frequency, attn_weights, valid_mask,
     """``(scores, indices)`` from one native call: the composition
     ``select_eviction_candidates(eviction_scores(...), k)``."""
     C = _lib()
+    if _all_cuda(recency, frequency, attn_weights, valid_mask):
+        return C.eviction_scores_select(recency, frequency, attn_weights, valid_mask, int(k),
+                                        w_recency, w_frequency, w_attention)
     st = _Staging(recency, frequency, attn_weights, valid_mask)
     scores, idx = C.eviction_scores_select(st.to_device(recency, torch.float32),
                                            st.to_device(frequency, torch.float32),
