@@ -581,6 +581,749 @@ __global__ void __launch_bounds__(kFastThreads, 2)
 }
 
 // ===========================================================================
+// Stream kernel: persistent CTAs over a balanced share of all pages
+// ===========================================================================
+//
+// The split kernel above gives every (sequence, split) its own CTA, so a
+// batch whose splits do not fill whole waves of the GPU (64 sequences of
+// 2,048 tokens: 1,024 CTAs for 296 slots) idles SMs in the last wave, and
+// every short CTA pays the block-table / scale / query prologue.  Here the
+// grid is ~2 CTAs per SM.  All pages of all (sequence, KV-head group) units
+// form one flattened range; CTA c takes pages [P*c/C, P*(c+1)/C), walks
+// them in chunks of <= kMaxTok tokens (K pages, softmax, V pages, as
+// above) and merges consecutive chunks of one unit with the online-softmax
+// rescale.
+//
+// A table warp fills a double-buffered chunk table (block-table entries,
+// scales, token count and, for a new unit, the query rows by bulk copy) and
+// publishes each half with an mbarrier (meta_full).  It fetches the first
+// two chunks together before any page load is issued, so these small loads
+// do not queue behind the GPU-wide burst of page loads, and later chunks
+// one chunk ahead.  The TMA warp then only waits for a chunk's table before
+// issuing its K and V pages back to back.  The per-head maximum of a
+// chunk's logits is gathered while the K pages are read, so the softmax is
+// a single vectorised pass.
+//
+// A unit owned by one CTA is written directly.  A unit that straddles CTAs
+// leaves one partial (acc, m, l) per CTA at slot unit + c; the CTA whose
+// arrival on the unit's counter completes the set merges them in segment
+// order (so the result does not depend on which CTA arrives last) and
+// writes the output.  The counters are zeroed on the stream before launch.
+
+constexpr int kStreamMaxSeqs = 1024;
+constexpr int kStreamThreads = kConsumers + 64;  // + TMA warp + table warp
+constexpr int kTmaWarp = kConsumerWarps;
+constexpr int kTableWarp = kConsumerWarps + 1;
+
+template <int BS, int HG, int G>
+struct StreamCfg {
+  using F = FastCfg<BS, HG, G>;
+  // one half of the double-buffered chunk table
+  static constexpr int kMetaPhys = 0;                                  // int [kMaxPages]
+  static constexpr int kMetaKs = kMetaPhys + F::kMaxPages * 4;         // float [kMaxPages][HG]
+  static constexpr int kMetaVs = kMetaKs + F::kMaxPages * HG * 4;      // float [kMaxPages][HG]
+  static constexpr int kMetaVmax = kMetaVs + F::kMaxPages * HG * 4;    // float [HG]
+  static constexpr int kMetaT = kMetaVmax + 32;                        // int: tokens in chunk
+  static constexpr int kMetaQ = (kMetaT + 4 + 15) & ~15;               // float [kNHG][kQRow]
+  static constexpr int kQRow = 132;  // padded row: spreads the halves' banks
+  // query rows staged only for G == 1 (larger groups read them from L2 into
+  // their digit table, which keeps two CTAs per SM within shared memory)
+  static constexpr int kMetaBytes = (kMetaQ + (G == 1 ? F::kNHG * kQRow * 4 : 0) + 15) & ~15;
+
+  // per query head a row of kMaxTok fp32 logits; the softmax overwrites its
+  // first 3 * kMaxTok bytes with the 24-bit probability planes
+  static constexpr int kOffLogit = kFastStages * kStageBytes;
+  static constexpr int kOffQd = kOffLogit + F::kNHG * F::kMaxTok * 4;
+  static constexpr int kOffQs = kOffQd + F::kNHG * F::kQdStride;
+  static constexpr int kOffRun = kOffQs + 64;   // float2 [16]: running (m, l)
+  static constexpr int kOffAB = kOffRun + 128;  // float2 [16]: (old-acc factor, chunk factor)
+  static constexpr int kOffMax = kOffAB + 128;  // uint [16]: chunk logit maximum (ordered key)
+  static constexpr int kOffTmp = kOffMax + 64;  // int [32] scan scratch, flag
+  static constexpr int kOffMeta = kOffTmp + 144;
+  static constexpr int kOffPseq = kOffMeta + 2 * kMetaBytes;
+  static constexpr int kOffRed = (kOffPseq + (kStreamMaxSeqs + 1) * 4 + 15) & ~15;
+  static constexpr int kRedBytes = F::kVR > 1 ? kConsumerWarps * F::kGPW * 128 * 4 : 0;
+  static constexpr int kOffBar = (kOffRed + kRedBytes + 15) & ~15;
+  static constexpr int kSmemBytes = kOffBar + (2 * kFastStages + 4) * 8 + 1024;
+  // two CTAs per SM (228 KB of shared memory, 1 KB reserved per CTA)
+  static_assert(2 * (kSmemBytes + 1024) <= 228 * 1024, "stream kernel shared memory");
+  static_assert(F::kMaxPages <= 32, "one chunk page per table-warp lane");
+  static_assert(kOffMeta % 16 == 0 && kMetaBytes % 16 == 0 && kMetaQ % 16 == 0 &&
+                    (kQRow * 4) % 16 == 0,
+                "bulk copies into the chunk table need 16-byte alignment");
+};
+
+struct StreamChunk {
+  int s, g;       // unit: sequence, KV-head group
+  int lp0, np;    // first page within the unit, pages in the chunk
+  bool seg_first, seg_last, whole;
+};
+
+// Walks one CTA's flattened page range [pos, end) in chunks of at most
+// max_pages pages; every thread of the CTA runs its own copy identically.
+struct StreamIter {
+  long long pos, end, cta_start;
+  int s, g, S, ng, max_pages;
+  const int* pseq;
+
+  __device__ void init(long long start, long long stop, const int* ps, int num_seqs, int groups,
+                       int mp) {
+    pos = start;
+    end = stop;
+    cta_start = start;
+    pseq = ps;
+    S = num_seqs;
+    ng = groups;
+    max_pages = mp;
+    s = 0;
+    g = 0;
+    if (pos >= end) return;
+    int lo = 0, hi = S - 1;  // largest s with pseq[s] * ng <= pos
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if ((long long)pseq[mid] * ng <= pos) lo = mid; else hi = mid - 1;
+    }
+    s = lo;
+    const int pages = pseq[s + 1] - pseq[s];
+    g = (int)((pos - (long long)pseq[s] * ng) / pages);
+  }
+
+  __device__ bool next(StreamChunk& c) {
+    if (pos >= end) return false;
+    const int pages = pseq[s + 1] - pseq[s];
+    const long long ustart = (long long)pseq[s] * ng + (long long)g * pages;
+    const int lp0 = (int)(pos - ustart);
+    const long long seg_lo_abs = cta_start > ustart ? cta_start : ustart;
+    const int seg_lo = (int)(seg_lo_abs - ustart);
+    const long long uend = ustart + pages;
+    const int seg_hi = (int)((end < uend ? end : uend) - ustart);
+    const int np = min(max_pages, seg_hi - lp0);
+    c.s = s;
+    c.g = g;
+    c.lp0 = lp0;
+    c.np = np;
+    c.seg_first = lp0 == seg_lo;
+    c.seg_last = lp0 + np == seg_hi;
+    c.whole = seg_lo == 0 && seg_hi == pages;
+    pos += np;
+    if (c.seg_last && pos < end) {
+      if (++g == ng) {
+        g = 0;
+        do {
+          ++s;
+        } while (s < S - 1 && pseq[s + 1] == pseq[s]);
+      }
+    }
+    return true;
+  }
+};
+
+// Ordered-integer image of a float for atomicMax (NaN never reaches it).
+__device__ __forceinline__ uint32_t float_max_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float float_from_max_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+constexpr uint32_t kNegInfKey = 0x007fffffu;  // float_max_key(-inf)
+
+// First and last CTA of a C-CTA split of P flattened pages that own pages
+// of [lo, lo + n).
+__device__ __forceinline__ int page_owner(long long x, long long P, int C) {
+  return (int)(((x + 1) * C - 1) / P);
+}
+__device__ __forceinline__ bool cta_owns_pages(long long P, int c, int C) {
+  return P * c / C < P * (c + 1) / C;
+}
+
+template <int BS, int HG, int G>
+__global__ void __launch_bounds__(kStreamThreads, 2)
+    decode_stream_kernel(const __grid_constant__ CUtensorMap map_k,
+                         const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q,
+                         const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+                         const int32_t* __restrict__ block_tables,
+                         const int32_t* __restrict__ seq_lens, float* __restrict__ out,
+                         float* __restrict__ ws_acc, float2* __restrict__ ws_ml,
+                         int* __restrict__ unit_arrivals, int num_seqs, int num_heads,
+                         int num_kv_heads, int64_t num_blocks, int max_blocks_per_seq,
+                         float qk_scale, int* err) {
+  using F = FastCfg<BS, HG, G>;
+  using C = StreamCfg<BS, HG, G>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* s_logit = reinterpret_cast<float*>(smem + C::kOffLogit);
+  float* s_qs = reinterpret_cast<float*>(smem + C::kOffQs);
+  float2* s_run = reinterpret_cast<float2*>(smem + C::kOffRun);
+  float2* s_ab = reinterpret_cast<float2*>(smem + C::kOffAB);
+  uint32_t* s_max = reinterpret_cast<uint32_t*>(smem + C::kOffMax);
+  int* s_tmp = reinterpret_cast<int*>(smem + C::kOffTmp);
+  int* s_pseq = reinterpret_cast<int*>(smem + C::kOffPseq);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + kFastStages;
+  uint64_t* meta_full = empty + kFastStages;  // [2]: chunk table half published
+  uint64_t* chunk_free = meta_full + 2;       // [2]: chunk table half released
+  const uint32_t stage_base = smem_u32(smem);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int S = num_seqs;
+  const int ng = num_kv_heads / HG;
+  const int n_ctas = gridDim.x;
+
+  // ---- pages per sequence and their prefix (every CTA, identically) -------
+  constexpr int kPer = (kStreamMaxSeqs + kStreamThreads - 1) / kStreamThreads;
+  int mine[kPer];
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int s = tid * kPer + i;
+    mine[i] = 0;
+    if (s < S) {
+      const int L = seq_lens[s];
+      mine[i] = covered_pages(L, BS, max_blocks_per_seq);
+      if (blockIdx.x == 0 && L > mine[i] * BS) record_error(err, kDevSeqTooLong);
+    }
+    sum += mine[i];
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) s_tmp[warp] = incl;
+  if (tid == 0) {
+    for (int i = 0; i < kFastStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumerWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&meta_full[i], 1);
+      mbar_init(&chunk_free[i], 2);  // consumers (softmax done) + TMA warp (pages issued)
+    }
+    mbar_fence_init();
+  }
+  if (tid < F::kNHG) s_max[tid] = kNegInfKey;
+  __syncthreads();
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += s_tmp[w];
+  int run = before + incl - sum;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int s = tid * kPer + i;
+    if (s <= S) s_pseq[s] = run;  // s == S: total
+    run += mine[i];
+  }
+  __syncthreads();
+  // sequences without pages: zero output (no unit covers them)
+  for (int s = blockIdx.x; s < S; s += n_ctas) {
+    if (s_pseq[s + 1] != s_pseq[s]) continue;
+    float4* o = reinterpret_cast<float4*>(out + (int64_t)s * num_heads * 128);
+    for (int i = tid; i < num_heads * 32; i += kStreamThreads) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const long long P = (long long)s_pseq[S] * ng;
+  const long long c_begin = P * blockIdx.x / n_ctas;
+  const long long c_end = P * (blockIdx.x + 1) / n_ctas;
+  if (c_begin >= c_end) return;  // uniform
+
+  StreamIter it;
+  it.init(c_begin, c_end, s_pseq, S, ng, F::kMaxPages);
+  StreamChunk ch;
+
+  // ---- table warp: chunk tables one chunk ahead ---------------------------
+  if (warp == kTableWarp) {
+    // block-table entry of this lane's page of chunk c (-1: none / invalid)
+    auto load_phys = [&](const StreamChunk& c) {
+      int phys = -1;
+      if (lane < c.np) {
+        const int v = block_tables[(int64_t)c.s * max_blocks_per_seq + c.lp0 + lane];
+        const bool ok = v >= 0 && (int64_t)v < num_blocks;
+        if (!ok) record_error(err, kDevBadBlockId);
+        phys = ok ? v : -1;
+      }
+      return phys;
+    };
+    auto load_scales = [&](const StreamChunk& c, int phys, float (&ks)[HG], float (&vs)[HG]) {
+      const int64_t si = (int64_t)(phys >= 0 ? phys : 0) * num_kv_heads + c.g * HG;
+#pragma unroll
+      for (int jj = 0; jj < HG; ++jj) {
+        ks[jj] = phys >= 0 ? k_scale[si + jj] : 0.0f;
+        vs[jj] = phys >= 0 ? v_scale[si + jj] : 0.0f;
+      }
+    };
+    // Writes chunk c's table into half b and publishes it on meta_full[b].
+    auto publish = [&](int b, const StreamChunk& c, bool new_unit, int phys,
+                       const float (&ks)[HG], const float (&vs)[HG]) {
+      uint8_t* meta = smem + C::kOffMeta + b * C::kMetaBytes;
+      if (lane < c.np) {
+        reinterpret_cast<int*>(meta + C::kMetaPhys)[lane] = phys;
+#pragma unroll
+        for (int jj = 0; jj < HG; ++jj) {
+          reinterpret_cast<float*>(meta + C::kMetaKs)[lane * HG + jj] = ks[jj];
+          reinterpret_cast<float*>(meta + C::kMetaVs)[lane * HG + jj] = vs[jj];
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < HG; ++jj) {
+        const float v = warp_max(vs[jj]);
+        if (lane == 0) reinterpret_cast<float*>(meta + C::kMetaVmax)[jj] = v;
+      }
+      if (lane == 0) {
+        const int pages = s_pseq[c.s + 1] - s_pseq[c.s];
+        const int Ls = min(max(seq_lens[c.s], 0), pages * BS);
+        *reinterpret_cast<int*>(meta + C::kMetaT) = min(Ls, (c.lp0 + c.np) * BS) - c.lp0 * BS;
+      }
+      const float* qu = q + ((int64_t)c.s * num_heads + (int64_t)c.g * F::kNHG) * 128;
+      if constexpr (G == 1) {
+        if (new_unit) {
+          if (lane == 0) mbar_expect_tx(&meta_full[b], F::kNHG * 512);
+          __syncwarp();
+          if (lane < F::kNHG)
+            bulk_load_g2s(meta + C::kMetaQ + lane * C::kQRow * 4, qu + lane * 128, 512,
+                          &meta_full[b]);
+        }
+      } else {
+        if (new_unit)
+          for (int ln = lane; ln < F::kNHG * 4; ln += 32)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(qu + ln * 32));
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_full[b]);
+    };
+    StreamChunk c0, c1;
+    const bool have0 = it.next(c0);
+    const bool have1 = have0 && it.next(c1);
+    if (!have0) return;
+    {  // the first two chunks, loads interleaved
+      float ks0[HG], vs0[HG], ks1[HG], vs1[HG];
+      const int p0 = load_phys(c0);
+      const int p1 = have1 ? load_phys(c1) : -1;
+      load_scales(c0, p0, ks0, vs0);
+      if (have1) load_scales(c1, p1, ks1, vs1);
+      publish(0, c0, true, p0, ks0, vs0);
+      if (have1) publish(1, c1, c1.s != c0.s || c1.g != c0.g, p1, ks1, vs1);
+    }
+    if (!have1) return;
+    StreamChunk prev = c1, cur;
+    for (int i = 2; it.next(cur); ++i) {
+      const int b = i & 1;
+      bool ok = true;
+      if (lane == 0 && !mbar_wait_bounded(&chunk_free[b], (uint32_t)((i >> 1) - 1) & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        ok = false;
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      float ks[HG], vs[HG];
+      const int ph = load_phys(cur);
+      load_scales(cur, ph, ks, vs);
+      publish(b, cur, cur.s != prev.s || cur.g != prev.g, ph, ks, vs);
+      prev = cur;
+    }
+    return;
+  }
+
+  // ---- TMA warp: K then V pages of each chunk -------------------------------
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+      int ns = 0;
+      for (int i = 0; it.next(ch); ++i) {
+        const int b = i & 1;
+        if (!mbar_wait_bounded(&meta_full[b], (uint32_t)(i >> 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          break;
+        }
+        const int* m_phys =
+            reinterpret_cast<const int*>(smem + C::kOffMeta + b * C::kMetaBytes + C::kMetaPhys);
+        const int n_st = (ch.np + F::kPPS - 1) / F::kPPS;
+        bool ok_run = true;
+        for (int kind = 0; kind < 2 && ok_run; ++kind) {
+          for (int st = 0; st < n_st; ++st, ++ns) {
+            const int slot = ns % kFastStages;
+            const uint32_t ph = (uint32_t)(ns / kFastStages) & 1u;
+            if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, err)) {
+              record_error(err, kDevWaitTimeout);
+              ok_run = false;
+              break;
+            }
+            const int pb = st * F::kPPS;
+            const int pe = min(ch.np, pb + F::kPPS);
+            mbar_arrive_expect_tx(&full[slot], (uint32_t)((pe - pb) * F::kPageBytes));
+            for (int pg = pb; pg < pe; ++pg)
+              tma_load_3d(smem + slot * kStageBytes + (pg - pb) * F::kPageBytes,
+                          kind ? &map_v : &map_k, &full[slot], 0, ch.g * HG,
+                          max(m_phys[pg], 0) * BS, policy);
+          }
+        }
+        if (!ok_run) break;
+        mbar_arrive(&chunk_free[b]);  // this warp is done with the chunk's table
+      }
+    }
+    return;
+  }
+
+  // ---- consumers -------------------------------------------------------------
+  const int k_line = tid >> 1;  // K phase: two threads per cache line
+  const int k_half = tid & 1;
+  const int k_jj = k_line % HG;
+  const int unit = warp % F::kUnits;  // p.V work unit (kv head, query-head pair)
+  const int v_r = warp / F::kUnits;
+  const int v_jj = unit / (G / F::kGPW);
+  const int g0 = (unit % (G / F::kGPW)) * F::kGPW;
+  const uint32_t word_off = (uint32_t)((lane & 3) << 2);
+  const int wchunk = lane >> 2;
+  float acc_run[F::kGPW][4];
+#pragma unroll
+  for (int g = 0; g < F::kGPW; ++g) acc_run[g][0] = acc_run[g][1] = acc_run[g][2] = acc_run[g][3] = 0.0f;
+  bool live = true;
+  int ns = 0, cur_s = -1, cur_g = -1;
+  for (int i = 0; it.next(ch); ++i) {
+    const uint8_t* meta = smem + C::kOffMeta + (i & 1) * C::kMetaBytes;
+    const int* m_phys = reinterpret_cast<const int*>(meta + C::kMetaPhys);
+    const float* m_ks = reinterpret_cast<const float*>(meta + C::kMetaKs);
+    const float* m_vs = reinterpret_cast<const float*>(meta + C::kMetaVs);
+    const float* m_q = reinterpret_cast<const float*>(meta + C::kMetaQ);
+    if (live && !mbar_wait_bounded(&meta_full[i & 1], (uint32_t)(i >> 1) & 1u, err)) {
+      record_error(err, kDevWaitTimeout);
+      live = false;
+    }
+    const int j0 = ch.g * HG;
+    const int T = live ? *reinterpret_cast<const int*>(meta + C::kMetaT) : 0;
+    const int n_st = (ch.np + F::kPPS - 1) / F::kPPS;
+
+    // every warp is past the previous chunk's V phase (which reads the
+    // probability planes) before this chunk's logits overwrite them
+    named_barrier(1, kConsumers);
+    if (ch.s != cur_s || ch.g != cur_g) {  // a new unit: its query digits
+      {
+        uint8_t* s_qd = smem + C::kOffQd;
+        const float* qu = q + ((int64_t)ch.s * num_heads + (int64_t)j0 * G) * 128;
+        for (int hg = warp; hg < F::kNHG; hg += kConsumerWarps) {
+          const float4 x = G == 1 ? reinterpret_cast<const float4*>(m_q + hg * C::kQRow)[lane]
+                                  : reinterpret_cast<const float4*>(qu + hg * 128)[lane];
+          float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+          m = warp_max(m);
+          const float inv = m > 0.0f ? (float)kQFix / m : 0.0f;
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+          int d[4][3];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            int n = __float2int_rn(xs[e] * inv);
+            n = max(-kQFix, min(kQFix, n));
+            to_digits(n, d[e][0], d[e][1], d[e][2]);
+          }
+#pragma unroll
+          for (int j = 0; j < 3; ++j)
+            reinterpret_cast<uint32_t*>(s_qd + hg * F::kQdStride + j * 128)[lane] =
+                pack4(d[0][j], d[1][j], d[2][j], d[3][j]);
+          if (lane == 0) s_qs[hg] = m > 0.0f ? m / (float)kQFix : 0.0f;
+        }
+        named_barrier(1, kConsumers);
+      }
+      cur_s = ch.s;
+      cur_g = ch.g;
+    }
+
+    // ---- K phase: logits, and this thread's running maximum per head ----
+    float kmax[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) kmax[g] = -INFINITY;
+    for (int st = 0; st < n_st; ++st, ++ns) {
+      const int slot = ns % kFastStages;
+      const uint32_t ph = (uint32_t)(ns / kFastStages) & 1u;
+      if (live && !mbar_wait_bounded(&full[slot], ph, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
+      }
+      if (live) {
+        const int tok = st * F::kTokPerStage + k_line / HG;
+        const uint32_t line_addr = stage_base + slot * kStageBytes + k_line * 128;
+        int acc[G][3];
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = 0;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = k_half * 4 + cc;
+          const uint4 kw = lds128(line_addr + ((c ^ (k_line & 7)) << 4));
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+              const uint4 qw = lds128(smem_u32(smem + C::kOffQd + (k_jj * G + g) * F::kQdStride +
+                                               j * 128 + c * 16));
+              int a = acc[g][j];
+              a = __dp4a((int)kw.x, (int)qw.x, a);
+              a = __dp4a((int)kw.y, (int)qw.y, a);
+              a = __dp4a((int)kw.z, (int)qw.z, a);
+              a = __dp4a((int)kw.w, (int)qw.w, a);
+              acc[g][j] = a;
+            }
+          }
+        }
+        const int pg = min(tok / BS, F::kMaxPages - 1);
+        const bool valid = tok < T && m_phys[pg] >= 0;
+        const float ks = m_ks[pg * HG + k_jj];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float part =
+              (float)acc[g][2] * 65536.0f + ((float)acc[g][1] * 256.0f + (float)acc[g][0]);
+          part += __shfl_xor_sync(0xffffffffu, part, 1);
+          const float qsv = s_qs[k_jj * G + g];
+          const float logit = valid ? part * (qsv * ks * qk_scale) : -INFINITY;
+          if (k_half == 0 && tok < T) {
+            s_logit[(k_jj * G + g) * F::kMaxTok + tok] = logit;
+            kmax[g] = fmaxf(kmax[g], logit);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    // lanes 2*HG*m apart hold the same head; lanes with (lane >> 1) < HG, even, publish
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int o = 2 * HG; o < 32; o <<= 1)
+        kmax[g] = fmaxf(kmax[g], __shfl_xor_sync(0xffffffffu, kmax[g], o));
+      if (k_half == 0 && (lane >> 1) < HG && kmax[g] != -INFINITY)
+        atomicMax(&s_max[k_jj * G + g], float_max_key(kmax[g]));
+    }
+    named_barrier(1, kConsumers);
+
+    // ---- softmax of the chunk, merged with the unit's running state ----
+    for (int hg = warp; hg < F::kNHG; hg += kConsumerWarps) {
+      const float4* row = reinterpret_cast<const float4*>(s_logit + hg * F::kMaxTok);
+      const float m = float_from_max_key(s_max[hg]);
+      const int jj = hg / G;
+      const float vmax = reinterpret_cast<const float*>(meta + C::kMetaVmax)[jj];
+      const float to_fix = vmax > 0.0f ? 16777215.0f / vmax : 0.0f;
+      uint8_t* pd = reinterpret_cast<uint8_t*>(s_logit + hg * F::kMaxTok);
+      constexpr int kIt = F::kMaxTok / 128;
+      const int T4q = (T + 3) >> 2;
+      float4 x[kIt];  // the whole row first: the planes overwrite it
+#pragma unroll
+      for (int k4 = 0; k4 < kIt; ++k4) {
+        const int t4 = lane + 32 * k4;
+        x[k4] = t4 < T4q ? row[t4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      __syncwarp();
+      float l = 0.0f;
+#pragma unroll
+      for (int k4 = 0; k4 < kIt; ++k4) {
+        const int t4 = lane + 32 * k4;
+        if (t4 < T4q) {
+          const int t = t4 * 4;
+          const float xs[4] = {x[k4].x, x[k4].y, x[k4].z, x[k4].w};
+          const float vs = m_vs[(t / BS) * HG + jj];
+          uint32_t n[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            n[e] = 0;
+            if (t + e < T && m != -INFINITY) {
+              const float p = exp2f(xs[e] - m);
+              l += p;
+              n[e] = __float2uint_rn(fminf(p * vs * to_fix, 16777215.0f));
+            }
+          }
+          const uint32_t lo01 = __byte_perm(n[0], n[1], 0x5140), hi01 = __byte_perm(n[0], n[1], 0x7362);
+          const uint32_t lo23 = __byte_perm(n[2], n[3], 0x5140), hi23 = __byte_perm(n[2], n[3], 0x7362);
+          *reinterpret_cast<uint32_t*>(pd + t) = __byte_perm(lo01, lo23, 0x5410);
+          *reinterpret_cast<uint32_t*>(pd + F::kMaxTok + t) = __byte_perm(lo01, lo23, 0x7632);
+          *reinterpret_cast<uint32_t*>(pd + 2 * F::kMaxTok + t) = __byte_perm(hi01, hi23, 0x5410);
+        }
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        const float2 r = ch.seg_first ? make_float2(-INFINITY, 0.0f) : s_run[hg];
+        const float mn = fmaxf(r.x, m);
+        const float a = (r.x == -INFINITY) ? 0.0f : exp2f(r.x - mn);
+        const float b = (m == -INFINITY) ? 0.0f : exp2f(m - mn);
+        s_run[hg] = make_float2(mn, r.y * a + l * b);
+        s_ab[hg] = make_float2(a, b * vmax * (1.0f / 16777215.0f));
+        s_max[hg] = kNegInfKey;
+      }
+    }
+    named_barrier(1, kConsumers);
+    if (tid == 0) mbar_arrive(&chunk_free[i & 1]);  // the chunk's table half is free
+
+    // ---- V phase: integer p.V ----
+    int iacc[F::kGPW][3][4];
+#pragma unroll
+    for (int g = 0; g < F::kGPW; ++g)
+#pragma unroll
+      for (int j = 0; j < 3; ++j) iacc[g][j][0] = iacc[g][j][1] = iacc[g][j][2] = iacc[g][j][3] = 0;
+    for (int st = 0; st < n_st; ++st, ++ns) {
+      const int slot = ns % kFastStages;
+      const uint32_t ph = (uint32_t)(ns / kFastStages) & 1u;
+      if (live && !mbar_wait_bounded(&full[slot], ph, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
+      }
+      if (live) {
+        const uint32_t base = stage_base + slot * kStageBytes;
+        const int tok0 = st * F::kTokPerStage;
+        const int ngroups = (min(F::kTokPerStage, T - tok0) + 3) >> 2;
+#pragma unroll 2
+        for (int gi = v_r; gi < ngroups; gi += F::kVR) {
+          const int ts = gi * 4;
+          uint32_t w[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int line = (ts + u) * HG + v_jj;
+            w[u] = lds32(base + line * 128 + ((wchunk ^ (line & 7)) << 4) + word_off);
+          }
+          const uint32_t t0 = __byte_perm(w[0], w[1], 0x5140), t1 = __byte_perm(w[0], w[1], 0x7362);
+          const uint32_t t2 = __byte_perm(w[2], w[3], 0x5140), t3 = __byte_perm(w[2], w[3], 0x7362);
+          const uint32_t cw[4] = {__byte_perm(t0, t2, 0x5410), __byte_perm(t0, t2, 0x7632),
+                                  __byte_perm(t1, t3, 0x5410), __byte_perm(t1, t3, 0x7632)};
+#pragma unroll
+          for (int g = 0; g < F::kGPW; ++g) {
+            const uint8_t* pd = reinterpret_cast<const uint8_t*>(s_logit + (v_jj * G + g0 + g) * F::kMaxTok) + tok0 + ts;
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+              const uint32_t pw = lds32(smem_u32(pd + j * F::kMaxTok));
+#pragma unroll
+              for (int c4 = 0; c4 < 4; ++c4) iacc[g][j][c4] = dp4a_su(cw[c4], pw, iacc[g][j][c4]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+#pragma unroll
+    for (int g = 0; g < F::kGPW; ++g) {
+      const float2 ab = s_ab[v_jj * G + g0 + g];
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4)
+        acc_run[g][c4] = acc_run[g][c4] * ab.x +
+                         ab.y * ((float)iacc[g][2][c4] * 65536.0f +
+                                 ((float)iacc[g][1][c4] * 256.0f + (float)iacc[g][0][c4]));
+    }
+
+    // ---- end of this CTA's part of the unit: write it ----
+    if (ch.seg_last) {
+      if constexpr (F::kVR > 1) {
+        float* red = reinterpret_cast<float*>(smem + C::kOffRed);
+#pragma unroll
+        for (int g = 0; g < F::kGPW; ++g)
+          reinterpret_cast<float4*>(red + ((v_r * F::kUnits + unit) * F::kGPW + g) * 128)[lane] =
+              make_float4(acc_run[g][0], acc_run[g][1], acc_run[g][2], acc_run[g][3]);
+        named_barrier(1, kConsumers);
+        if (v_r == 0) {
+#pragma unroll
+          for (int g = 0; g < F::kGPW; ++g) {
+            for (int r = 1; r < F::kVR; ++r) {
+              const float4 o = reinterpret_cast<const float4*>(
+                  red + ((r * F::kUnits + unit) * F::kGPW + g) * 128)[lane];
+              acc_run[g][0] += o.x;
+              acc_run[g][1] += o.y;
+              acc_run[g][2] += o.z;
+              acc_run[g][3] += o.w;
+            }
+          }
+        }
+      }
+      const int u = ch.s * ng + ch.g;
+      if (ch.whole) {
+        if (v_r == 0) {
+#pragma unroll
+          for (int g = 0; g < F::kGPW; ++g) {
+            const int hg = v_jj * G + g0 + g;
+            const float2 ml = s_run[hg];
+            const float inv = ml.y > 0.0f ? 1.0f / ml.y : 0.0f;
+            reinterpret_cast<float4*>(out + ((int64_t)ch.s * num_heads + (int64_t)j0 * G + hg) * 128)[lane] =
+                make_float4(acc_run[g][0] * inv, acc_run[g][1] * inv, acc_run[g][2] * inv,
+                            acc_run[g][3] * inv);
+          }
+        }
+      } else {
+        if (v_r == 0) {
+#pragma unroll
+          for (int g = 0; g < F::kGPW; ++g) {
+            const int hg = v_jj * G + g0 + g;
+            const int64_t slot = ((int64_t)u + blockIdx.x) * F::kNHG + hg;
+            reinterpret_cast<float4*>(ws_acc + slot * 128)[lane] =
+                make_float4(acc_run[g][0], acc_run[g][1], acc_run[g][2], acc_run[g][3]);
+            if (lane == 0) ws_ml[slot] = s_run[hg];
+          }
+          __threadfence();
+        }
+        // the unit's CTAs, in page order
+        const int pages = s_pseq[ch.s + 1] - s_pseq[ch.s];
+        const long long ustart = (long long)s_pseq[ch.s] * ng + (long long)ch.g * pages;
+        const int first = page_owner(ustart, P, n_ctas);
+        const int last = page_owner(ustart + pages - 1, P, n_ctas);
+        const bool all_own = P >= n_ctas;  // then every CTA owns >= 1 page
+        named_barrier(1, kConsumers);
+        if (tid == 0) {
+          int nseg = last - first + 1;
+          if (!all_own) {
+            nseg = 0;
+            for (int c = first; c <= last; ++c) nseg += cta_owns_pages(P, c, n_ctas);
+          }
+          const int done = atomicAdd(&unit_arrivals[u], 1) + 1;
+          s_tmp[32] = done == nseg;
+        }
+        named_barrier(1, kConsumers);
+        if (s_tmp[32] && v_r == 0) {  // this CTA completed the set: merge
+          __threadfence();
+#pragma unroll 1
+          for (int g = 0; g < F::kGPW; ++g) {
+            const int hg = v_jj * G + g0 + g;
+            auto slot_of = [&](int c) { return ((int64_t)u + c) * F::kNHG + hg; };
+            float M = -INFINITY;
+            for (int b = first; b <= last; b += 32) {
+              const int c = b + lane;
+              if (c <= last && (all_own || cta_owns_pages(P, c, n_ctas)))
+                M = fmaxf(M, __ldcg(&ws_ml[slot_of(c)]).x);
+            }
+            M = warp_max(M);
+            float den = 0.0f;
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int b = first; b <= last; b += 32) {
+              const int c = b + lane;
+              float w = 0.0f;
+              if (c <= last && (all_own || cta_owns_pages(P, c, n_ctas))) {
+                const float2 ml = __ldcg(&ws_ml[slot_of(c)]);
+                if (ml.x != -INFINITY) {
+                  w = exp2f(ml.x - M);
+                  den += w * ml.y;
+                }
+              }
+              const int nb = min(32, last - b + 1);
+#pragma unroll 4
+              for (int j = 0; j < nb; ++j) {
+                const float wj = __shfl_sync(0xffffffffu, w, j);
+                if (wj != 0.0f) {
+                  const float4 x = __ldcg(reinterpret_cast<const float4*>(ws_acc + slot_of(b + j) * 128) + lane);
+                  a.x += wj * x.x;
+                  a.y += wj * x.y;
+                  a.z += wj * x.z;
+                  a.w += wj * x.w;
+                }
+              }
+            }
+            den = warp_sum(den);
+            const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+            reinterpret_cast<float4*>(out + ((int64_t)ch.s * num_heads + (int64_t)j0 * G + hg) * 128)[lane] =
+                make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < F::kGPW; ++g) acc_run[g][0] = acc_run[g][1] = acc_run[g][2] = acc_run[g][3] = 0.0f;
+    }
+  }
+}
+
+// ===========================================================================
 // Generic kernel
 // ===========================================================================
 
@@ -728,10 +1471,25 @@ __global__ void __launch_bounds__(128)
 
 struct Plan {
   bool fast = false;
+  bool stream = false;  // persistent balanced kernel (fast shapes, S <= 1024)
   int hg = 1, g = 1;
   int pages_per_split = 1;
   int max_splits = 1;
+  int n_ctas = 0;  // stream kernel grid
 };
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
 
 int env_int(const char* name, int dflt) {
   const char* v = std::getenv(name);
@@ -779,7 +1537,30 @@ Plan make_plan(const DecodeArgs& a) {
     p.pages_per_split = pps;
   }
   p.max_splits = std::max(1, (M + p.pages_per_split - 1) / p.pages_per_split);
+  if (p.fast && a.num_seqs <= kStreamMaxSeqs && env_int("PKV_DECODE_SPLIT", 0) == 0) {
+    p.stream = true;
+    const int forced = env_int("PKV_DECODE_CTAS", 0);
+    p.n_ctas = forced > 0 ? forced : 2 * sm_count();
+  }
   return p;
+}
+
+// Workspace of the stream kernel: partial slots (units + CTAs) x query
+// heads per unit, then (m, l) per slot, then one arrival counter per unit.
+struct StreamWs {
+  size_t acc_off, ml_off, cnt_off, units, bytes;
+};
+
+StreamWs stream_ws_layout(const DecodeArgs& a, const Plan& p) {
+  const size_t units = (size_t)a.num_seqs * (a.num_kv_heads / p.hg);
+  const size_t slots = (units + p.n_ctas) * (size_t)(p.hg * p.g);
+  StreamWs w;
+  w.units = units;
+  w.acc_off = 0;
+  w.ml_off = (slots * 128 * sizeof(float) + 255) & ~(size_t)255;
+  w.cnt_off = (w.ml_off + slots * sizeof(float2) + 255) & ~(size_t)255;
+  w.bytes = w.cnt_off + units * sizeof(int) + 256;
+  return w;
 }
 
 template <int BS, int HG, int G>
@@ -792,12 +1573,28 @@ int launch_fast_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_
     set_error("cuTensorMapEncodeTiled failed for the paged cache");
     return kCudaError;
   }
-  auto kern = decode_fast_kernel<BS, HG, G>;
-  static bool attr_done = false;  // per instantiation
-  if (!attr_done) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    attr_done = true;
+  if (p.stream) {
+    using SC = StreamCfg<BS, HG, G>;
+    auto skern = decode_stream_kernel<BS, HG, G>;
+    cudaFuncSetAttribute(skern, cudaFuncAttributeMaxDynamicSharedMemorySize, SC::kSmemBytes);
+    const StreamWs w = stream_ws_layout(a, p);
+    uint8_t* base = reinterpret_cast<uint8_t*>(ws_acc);
+    float* sacc = reinterpret_cast<float*>(base + w.acc_off);
+    float2* sml = reinterpret_cast<float2*>(base + w.ml_off);
+    int* scnt = reinterpret_cast<int*>(base + w.cnt_off);
+    const cudaError_t me = cudaMemsetAsync(scnt, 0, w.units * sizeof(int), stream);
+    if (me != cudaSuccess) {
+      set_error(std::string("decode counter reset failed: ") + cudaGetErrorString(me));
+      return kCudaError;
+    }
+    skern<<<p.n_ctas, kStreamThreads, SC::kSmemBytes, stream>>>(
+        mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out, sacc, sml, scnt,
+        a.num_seqs, a.num_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq,
+        a.sm_scale * kLog2e, device_error_word());
+    return kOk;
   }
+  auto kern = decode_fast_kernel<BS, HG, G>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   dim3 grid(a.num_seqs, p.max_splits, a.num_kv_heads / HG);
   kern<<<grid, kFastThreads, C::kSmemBytes, stream>>>(
       mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out, ws_acc, ws_ml,
@@ -834,6 +1631,7 @@ int dispatch_hg(const DecodeArgs& a, const Plan& p, float* wa, float2* wm, cudaS
 
 size_t decode_workspace_size(const DecodeArgs& a) {
   const Plan p = make_plan(a);
+  if (p.stream) return stream_ws_layout(a, p).bytes;
   if (p.max_splits <= 1) return 0;
   const size_t slots = (size_t)a.num_seqs * p.max_splits * a.num_heads;
   return slots * a.head_dim * sizeof(float) + slots * sizeof(float2) + 256;
@@ -845,6 +1643,24 @@ int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
   const Plan p = make_plan(a);
   float* ws_acc = nullptr;
   float2* ws_ml = nullptr;
+  if (p.stream) {
+    const size_t need = stream_ws_layout(a, p).bytes;
+    if (workspace == nullptr || workspace_bytes < need) {
+      set_error("workspace too small for decode: need " + std::to_string(need) + " bytes");
+      return kWorkspace;
+    }
+    ws_acc = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) &
+                                      ~(uintptr_t)255);
+    const int rc = a.block_size == 16 ? dispatch_hg<16>(a, p, ws_acc, nullptr, stream)
+                                      : dispatch_hg<32>(a, p, ws_acc, nullptr, stream);
+    if (rc != kOk) return rc;
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_error(std::string("decode launch failed: ") + cudaGetErrorString(e));
+      return kCudaError;
+    }
+    return kOk;
+  }
   if (p.max_splits > 1) {
     const size_t need = decode_workspace_size(a);
     if (workspace == nullptr || workspace_bytes < need) {

@@ -71,6 +71,24 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
       : "memory");
 }
 
+// Raises the barrier's expected transaction bytes without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Bulk copy from global memory into this CTA's shared memory; the bytes
+// complete on bar.  Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile(
       "{\n\t.reg .b64 st;\n\t"
@@ -92,22 +110,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait that suspends the thread in hardware (up to hint_ns) until the
+// phase completes, so waiting warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity,
+                                                      uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after
 // `limit_ns` nanoseconds of wall time, or as soon as any CTA has recorded a
-// wait timeout in the error word (both checked every 64 polls), and returns
-// false; the caller records kDevWaitTimeout and unwinds.
+// wait timeout in the error word (both checked after every suspended poll of
+// at most 100 us), and returns false; the caller records kDevWaitTimeout and
+// unwinds.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   const int* err,
                                                   uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (global_timer_ns() - t0 > limit_ns) return false;
-      if (err != nullptr && *reinterpret_cast<const volatile int*>(err) == kDevWaitTimeout)
-        return false;
-    }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, 100000u)) return true;
+    if (global_timer_ns() - t0 > limit_ns) return false;
+    if (err != nullptr && *reinterpret_cast<const volatile int*>(err) == kDevWaitTimeout)
+      return false;
   }
 }
 

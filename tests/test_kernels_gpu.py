@@ -316,8 +316,35 @@ def test_attention_forced_generic_path_agrees(cuda, monkeypatch):
     assert_attention_close(slow, want)
 
 
+@pytest.mark.parametrize("ctas", ["1", "3", "7", "64", "500"])
+def test_attention_stream_grid_sizes(cuda, monkeypatch, ctas):
+    """Persistent stream kernel with few and many CTAs: units straddling
+    CTAs, several chunks and several units per CTA, idle CTAs."""
+    monkeypatch.setenv("PKV_DECODE_CTAS", ctas)
+    for seed, shape in ((11, (5, 8, 8, 128, 16, 1100)), (12, (9, 32, 8, 128, 16, 2500)),
+                        (13, (4, 4, 1, 128, 32, 3000))):
+        prob = problems.make_paged_kv_problem(np.random.default_rng(seed), *shape)
+        args = quantized_problem(*prob)
+        assert_attention_close(run_attention(args), c_oracle.paged_attention(*args))
+
+
+def test_attention_stream_one_sequence_over_all_ctas(cuda):
+    """One 12,288-token sequence: every CTA of the persistent grid holds a
+    slice of the same units, so the CTA completing a unit merges hundreds of
+    partials.  The merge runs in page order whichever CTA arrives last, so
+    repeated calls agree bit for bit."""
+    prob = problems.make_paged_kv_problem(np.random.default_rng(21), 1, 16, 8, 128, 16, 12288)
+    args = quantized_problem(*prob)
+    want = c_oracle.paged_attention(*args)
+    outs = [run_attention(args) for _ in range(3)]
+    assert_attention_close(outs[0], want)
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+
+
 @pytest.mark.parametrize("pages", ["1", "2", "8", "32"])
 def test_attention_split_sizes(cuda, monkeypatch, pages):
+    monkeypatch.setenv("PKV_DECODE_SPLIT", "1")
     monkeypatch.setenv("PKV_DECODE_SPLIT_PAGES", pages)
     prob = problems.make_paged_kv_problem(np.random.default_rng(11), 5, 8, 8, 128, 16, 1100)
     args = quantized_problem(*prob)

@@ -83,9 +83,9 @@ def test_noalloc_rejects_work_beyond_its_scratch():
     lib = _lib()
     cap = lib.pkv_noalloc_scratch_bytes()
     assert cap == 32 << 20
-    # 256 sequences x 40 heads of 8,192 tokens: ~85 MB of split-K partials;
-    # rejected on the host before any kernel is launched
-    S, H, D, bs, M = 256, 40, 128, 16, 512
+    # 2,048 sequences x 40 heads of 8,192 tokens: hundreds of MB of split-K
+    # partials; rejected on the host before any kernel is launched
+    S, H, D, bs, M = 2048, 40, 128, 16, 512
     q = torch.zeros(S, H, D, device="cuda")
     kq = torch.zeros(4, bs, H, D, dtype=torch.int8, device="cuda")
     ks = torch.ones(4, H, device="cuda")
