@@ -451,6 +451,20 @@ def run_gpu_arm(args):
                "note": "KV cache device-resident (serving state); per-step inputs and output "
                        "cross PCIe; wall clock per step, max over ranks"}
 
+    # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum)
+    # from one ncu capture of decode_stream_kernel<16, 8, 1> on the heavy-tail
+    # workload: 272,910,336 B for 269,517,056 algorithmic bytes.  A large-head
+    # launch (24 GB resident) is too large to capture; the same kernel streams
+    # the same per-page layout, so its traffic is that ratio times its own
+    # algorithmic bytes.
+    traffic = my_bytes * (272910336 / 269517056)
+    traffic_basis = ("ncu capture of this workload" if args.workload == "heavy-tail"
+                     else "heavy-tail ncu capture's traffic/algorithmic ratio x this "
+                          "workload's algorithmic bytes")
+    launches_per_step = C.quant_paged_attention_kernel_launches(
+        len(lens), heads, heads, HEAD_DIM, BLOCK, bt_np.shape[1])
+    plan_name = ("persistent decode_stream_kernel" if launches_per_step == 1
+                 else "split-K decode kernel + combine")
     result = None
     if rank == 0:
         peaks = {}
@@ -471,14 +485,15 @@ def run_gpu_arm(args):
                        "l2": "inputs larger than L2 (no flush)"},
             "kv_tokens_per_s": float(all_lens.sum()) / (ms_per_step / 1e3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": traffic,
+                         "traffic_unit": "bytes per launch", "traffic_basis": traffic_basis,
                          "basis": f"{my_bytes} algorithmic bytes per step on rank 0 / mean "
                                   "CUDA-event time of one quant_paged_attention call "
-                                  "(split-K kernel + combine)",
+                                  f"({launches_per_step} kernel launch(es): {plan_name})",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if pk.exists()
                          else "fallback 6650 GB/s"},
             "clocks": clocks, "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
         }
     # CPU baseline and the eviction latency on rank 0 at N = 1
     if rank == 0 and world == 1:

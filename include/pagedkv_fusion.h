@@ -145,7 +145,9 @@ int pkv_quantize_kv_per_block(const void *kv, int32_t kv_dtype, int8_t *q,
  * length 0 yields zeros.  Replaces quant_paged_attention_cuda
  * (csrc/quant_paged_attention.cu:172-225) bound at csrc/bindings.cpp:21-25.
  * Envelope: head_dim % 32 == 0 and <= 256, block_size <= 64,
- * num_heads % num_kv_heads == 0.  The workspace holds split-K partials.
+ * num_heads % num_kv_heads == 0.  The workspace holds the partial results
+ * of sequences whose pages are split across CTAs, and one arrival counter
+ * per (sequence, KV-head group) that the call resets on its stream.
  */
 size_t pkv_quant_paged_attention_workspace_size(
     int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
@@ -160,6 +162,19 @@ int pkv_quant_paged_attention(const float *q, const int8_t *k_cache,
                               int32_t max_blocks_per_seq, float sm_scale,
                               void *workspace, size_t workspace_bytes,
                               void *stream);
+
+/*
+ * Number of kernels one pkv_quant_paged_attention call with these shapes
+ * launches on its stream (16-byte aligned pointers): 1 for the persistent
+ * stream kernel (up to 1,024 sequences with head_dim 128, block_size 16 or
+ * 32 and a power-of-two GQA group <= 8), 2 for the split-K kernel and its
+ * combine.  Lets a caller account for launches without a profiler.  No
+ * counterpart in the reference.
+ */
+int pkv_quant_paged_attention_kernel_launches(int32_t num_seqs, int32_t num_heads,
+                                              int32_t num_kv_heads, int32_t head_dim,
+                                              int32_t block_size,
+                                              int32_t max_blocks_per_seq);
 
 /*
  * pkv_quant_paged_attention without a workspace argument, for callers that

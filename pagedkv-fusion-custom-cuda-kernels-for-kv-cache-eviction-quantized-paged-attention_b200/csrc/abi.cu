@@ -252,6 +252,17 @@ size_t pkv_quant_paged_attention_workspace_size(int32_t num_seqs, int32_t num_he
   return fast > gen ? fast : gen;
 }
 
+int pkv_quant_paged_attention_kernel_launches(int32_t num_seqs, int32_t num_heads,
+                                              int32_t num_kv_heads, int32_t head_dim,
+                                              int32_t block_size, int32_t max_blocks_per_seq) {
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || block_size <= 0) return 0;
+  const pkv::DecodeArgs a = decode_args(
+      reinterpret_cast<const float*>(16), reinterpret_cast<const int8_t*>(16), nullptr,
+      reinterpret_cast<const int8_t*>(16), nullptr, nullptr, nullptr, reinterpret_cast<float*>(16),
+      num_seqs, num_heads, num_kv_heads, head_dim, block_size, 1, max_blocks_per_seq, 1.0f);
+  return pkv::decode_kernel_launches(a);
+}
+
 int pkv_quant_paged_attention(const float* q, const int8_t* k_cache, const float* k_scale,
                               const int8_t* v_cache, const float* v_scale,
                               const int32_t* block_tables, const int32_t* seq_lens, float* out,

@@ -1637,6 +1637,11 @@ size_t decode_workspace_size(const DecodeArgs& a) {
   return slots * a.head_dim * sizeof(float) + slots * sizeof(float2) + 256;
 }
 
+int decode_kernel_launches(const DecodeArgs& a) {
+  if (a.num_seqs <= 0) return 0;
+  return make_plan(a).stream ? 1 : 2;  // stream kernel | split kernel + combine
+}
+
 int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
                   cudaStream_t stream) {
   if (a.num_seqs == 0) return kOk;

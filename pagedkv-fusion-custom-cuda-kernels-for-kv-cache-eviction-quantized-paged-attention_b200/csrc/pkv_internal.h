@@ -78,6 +78,8 @@ struct DecodeArgs {
 };
 
 size_t decode_workspace_size(const DecodeArgs& a);
+// Kernels one launch_decode call issues for these arguments.
+int decode_kernel_launches(const DecodeArgs& a);
 int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
                   cudaStream_t stream);
 

@@ -48,6 +48,7 @@ _merge_ws = _sig("pkv_eviction_merge_workspace_size", [_I64, _I64], _SZ)
 _merge = _sig("pkv_eviction_merge", [_P, _I64, _I64, _P, _P, _SZ, _P])
 _quant = _sig("pkv_quantize_kv_per_block", [_P, _I32, _P, _P, _I64, _I32, _I32, _I32, _P])
 _attn_ws = _sig("pkv_quant_paged_attention_workspace_size", [_I32] * 6, _SZ)
+_attn_launches = _sig("pkv_quant_paged_attention_kernel_launches", [_I32] * 6, ct.c_int)
 _attn = _sig("pkv_quant_paged_attention",
              [_P] * 8 + [_I32] * 5 + [_I64, _I32, _F, _P, _SZ, _P])
 _wtc_ws = _sig("pkv_write_to_cache_workspace_size", [_I64, _I32], _SZ)
@@ -169,6 +170,13 @@ def quant_paged_attention(q, k_cache_q, k_scale, v_cache_q, v_scale, block_table
 # ---------------------------------------------------------------------------
 # Entry points added by this build
 # ---------------------------------------------------------------------------
+
+def quant_paged_attention_kernel_launches(num_seqs, num_heads, num_kv_heads, head_dim, block_size,
+                                          max_blocks_per_seq):
+    """Kernels one quant_paged_attention call of these shapes launches."""
+    return int(_attn_launches(num_seqs, num_heads, num_kv_heads, head_dim, block_size,
+                              max_blocks_per_seq))
+
 
 def quantize_kv_per_block(kv, out_q=None, out_scale=None):
     """Native per-(block, head) INT8 quantization; see reference.py:88-105.

@@ -100,6 +100,21 @@ def test_decode_workspace_size(lib):
     assert f(0, 8, 8, 128, 16, 128) == 0
 
 
+def test_decode_kernel_launches_per_call(lib, monkeypatch):
+    f = lib.pkv_quant_paged_attention_kernel_launches
+    f.argtypes = [ct.c_int32] * 6
+    f.restype = ct.c_int
+    monkeypatch.delenv("PKV_DECODE_SPLIT", raising=False)
+    monkeypatch.delenv("PKV_DECODE_GENERIC", raising=False)
+    assert f(64, 8, 8, 128, 16, 128) == 1      # persistent stream kernel
+    assert f(512, 32, 8, 128, 16, 512) == 1    # GQA group of 4
+    assert f(2048, 8, 8, 128, 16, 128) == 2    # > 1,024 sequences: split-K + combine
+    assert f(8, 8, 8, 64, 16, 32) == 2         # head_dim 64: generic kernel + combine
+    assert f(0, 8, 8, 128, 16, 128) == 0
+    monkeypatch.setenv("PKV_DECODE_SPLIT", "1")
+    assert f(64, 8, 8, 128, 16, 128) == 2
+
+
 def test_quantize_rejects_bad_dtype(lib):
     f = lib.pkv_quantize_kv_per_block
     f.argtypes = [ct.c_void_p, ct.c_int32, ct.c_void_p, ct.c_void_p, ct.c_int64, ct.c_int32,
