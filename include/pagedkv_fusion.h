@@ -138,6 +138,47 @@ int pkv_quantize_kv_per_block(const void *kv, int32_t kv_dtype, int8_t *q,
                               int32_t head_dim, void *stream);
 
 /*
+ * pkv_quantize_kv_per_block for the blocks whose skip[b] byte is zero;
+ * blocks with a nonzero byte are neither read nor written (their codes and
+ * scale keep whatever they held).  Quantizes the blocks that survive an
+ * eviction without touching the evicted ones.  No counterpart in the
+ * reference: its end-to-end demo (scripts/run_end_to_end_demo.py:74-116)
+ * scores and selects, then quantizes every block and decodes over the
+ * unchanged tables.
+ */
+int pkv_quantize_kv_per_block_except(const void *kv, int32_t kv_dtype,
+                                     const uint8_t *skip, int8_t *q,
+                                     float *scale, int64_t num_blocks,
+                                     int32_t block_size, int32_t num_kv_heads,
+                                     int32_t head_dim, void *stream);
+
+/*
+ * mask[0 .. num_blocks) = 0, then mask[id - id_offset] = 1 for every id in
+ * ids[0 .. num_ids) that falls in [id_offset, id_offset + num_blocks): the
+ * local eviction mask of a rank holding blocks id_offset.. from the global
+ * ids a (sharded) selection returned.  No counterpart in the reference.
+ */
+int pkv_mark_blocks(const int64_t *ids, int64_t num_ids, int64_t id_offset,
+                    int64_t num_blocks, uint8_t *mask, void *stream);
+
+/*
+ * Removes evicted blocks from block tables.  For sequence s the first
+ * ceil(seq_lens[s] / block_size) entries (clamped to the table width;
+ * PKV_DEVERR_SEQ_TOO_LONG beyond it) are its pages, the last holding the
+ * remainder; pages whose block has evicted[id] != 0 are dropped, the rest
+ * are written in order to tables_out (row padded with -1) and lens_out[s]
+ * is the number of tokens they hold.  Every kept page but the last is full,
+ * so (tables_out, lens_out) is a valid input to pkv_quant_paged_attention.
+ * Ids outside [0, num_blocks) are kept.  No counterpart in the reference.
+ */
+int pkv_compact_block_tables(const int32_t *block_tables,
+                             const int32_t *seq_lens, const uint8_t *evicted,
+                             int32_t *tables_out, int32_t *lens_out,
+                             int32_t num_seqs, int32_t max_blocks_per_seq,
+                             int32_t block_size, int64_t num_blocks,
+                             void *stream);
+
+/*
  * Decode-step attention over the INT8 paged cache: out[s, h, :] =
  * softmax(q[s, h] . K^T * sm_scale) V over the seq_lens[s] tokens reached
  * through block_tables[s], dequantized with the per-(block, head) scales;

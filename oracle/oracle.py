@@ -46,6 +46,9 @@ __all__ = [
     "paged_attention",
     "dense_attention",
     "write_to_cache",
+    "mark_blocks",
+    "compact_block_tables",
+    "evict_quantize_decode",
 ]
 
 
@@ -262,3 +265,63 @@ def write_to_cache(key, value, kv_cache_int8, scale_cache, slot_mapping,
         kv_cache_int8[1, b, offs] = vq[0]
         scale_cache[0, b] = ks[0]
         scale_cache[1, b] = vs[0]
+
+
+# ---------------------------------------------------------------------------
+# Evict -> quantize -> decode composition.  The reference has no such step:
+# its demo (scripts/run_end_to_end_demo.py:74-116) scores and selects, then
+# quantizes every block and decodes over the unchanged tables.  These
+# functions define the composition the CUDA path implements, built from the
+# pinned functions above.
+# ---------------------------------------------------------------------------
+
+def mark_blocks(ids, id_offset: int, num_blocks: int) -> np.ndarray:
+    """uint8 mask with 1 at id - id_offset for the ids in this range."""
+    mask = np.zeros(int(num_blocks), dtype=np.uint8)
+    local = np.asarray(ids, dtype=np.int64) - int(id_offset)
+    mask[local[(local >= 0) & (local < num_blocks)]] = 1
+    return mask
+
+
+def compact_block_tables(block_tables, seq_lens, evicted, block_size: int):
+    """Drops evicted blocks from each sequence's pages, keeping order.
+
+    Page p of the first ceil(L/bs) (clamped to the table width) holds bs
+    tokens, the last one the remainder; the kept pages are written in order,
+    the rest of the row becomes -1, and the new length is the kept tokens.
+    Ids outside the mask's range are kept.
+    """
+    bt = np.asarray(block_tables, dtype=np.int32)
+    S, M = bt.shape
+    out = np.full_like(bt, -1)
+    lens = np.zeros(S, dtype=np.int32)
+    ev = np.asarray(evicted)
+    for s in range(S):
+        L = max(int(seq_lens[s]), 0)
+        pages = min((L + block_size - 1) // block_size, M)
+        kept, tokens = 0, 0
+        for p in range(pages):
+            bid = int(bt[s, p])
+            if 0 <= bid < ev.shape[0] and ev[bid]:
+                continue
+            out[s, kept] = bid
+            kept += 1
+            tokens += (min(L, pages * block_size) - p * block_size) if p == pages - 1 \
+                else block_size
+        lens[s] = tokens
+    return out, lens
+
+
+def evict_quantize_decode(q, k, v, recency, frequency, attn_weights, valid_mask,
+                          block_tables, seq_lens, num_evict: int, sm_scale):
+    """One composed step: score every block, evict the num_evict lowest
+    (score, id), quantize the cache, decode over the compacted tables.
+    Returns (out, evicted_ids, tables, lens)."""
+    scores = eviction_scores(recency, frequency, attn_weights, valid_mask)
+    ids = select_eviction_candidates(scores, num_evict)
+    mask = mark_blocks(ids, 0, k.shape[0])
+    kq, ks = quantize_kv_per_block(k)
+    vq, vs = quantize_kv_per_block(v)
+    tables, lens = compact_block_tables(block_tables, seq_lens, mask, k.shape[1])
+    out = paged_attention(q, kq, ks, vq, vs, tables, lens, sm_scale)
+    return out, ids, tables, lens

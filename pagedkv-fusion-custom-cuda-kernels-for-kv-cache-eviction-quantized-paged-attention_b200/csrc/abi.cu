@@ -172,10 +172,9 @@ int pkv_eviction_merge(const uint64_t* keys, int64_t num_keys, int64_t k, int64_
                             workspace_bytes, as_stream(stream));
 }
 
-int pkv_quantize_kv_per_block(const void* kv, int32_t kv_dtype, int8_t* q, float* scale,
-                              int64_t num_blocks, int32_t block_size, int32_t num_kv_heads,
-                              int32_t head_dim, void* stream) {
-  clear_error();
+static int quantize_checked(const void* kv, int32_t kv_dtype, int8_t* q, float* scale,
+                            int64_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                            int32_t head_dim, const uint8_t* skip, void* stream) {
   if (num_blocks < 0 || block_size < 0 || num_kv_heads < 0 || head_dim < 0)
     return fail(PKV_ERR_INVALID_ARGUMENT, "expected 4D [nb, bs, nkv, hd]");
   if (kv_dtype < 0 || kv_dtype > 2)
@@ -188,7 +187,48 @@ int pkv_quantize_kv_per_block(const void* kv, int32_t kv_dtype, int8_t* q, float
     return fail(PKV_ERR_UNSUPPORTED, "num_kv_heads too large");
   if (num_kv_heads == 0) return PKV_OK;
   return pkv::launch_quantize(kv, kv_dtype, q, scale, num_blocks, block_size, num_kv_heads,
-                              head_dim, as_stream(stream));
+                              head_dim, skip, as_stream(stream));
+}
+
+int pkv_quantize_kv_per_block(const void* kv, int32_t kv_dtype, int8_t* q, float* scale,
+                              int64_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                              int32_t head_dim, void* stream) {
+  clear_error();
+  return quantize_checked(kv, kv_dtype, q, scale, num_blocks, block_size, num_kv_heads, head_dim,
+                          nullptr, stream);
+}
+
+int pkv_quantize_kv_per_block_except(const void* kv, int32_t kv_dtype, const uint8_t* skip,
+                                     int8_t* q, float* scale, int64_t num_blocks,
+                                     int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                                     void* stream) {
+  clear_error();
+  if (num_blocks > 0 && !skip) return fail(PKV_ERR_INVALID_ARGUMENT, "null skip mask");
+  return quantize_checked(kv, kv_dtype, q, scale, num_blocks, block_size, num_kv_heads, head_dim,
+                          skip, stream);
+}
+
+int pkv_mark_blocks(const int64_t* ids, int64_t num_ids, int64_t id_offset, int64_t num_blocks,
+                    uint8_t* mask, void* stream) {
+  clear_error();
+  if (num_ids < 0 || num_blocks < 0) return fail(PKV_ERR_INVALID_ARGUMENT, "negative size");
+  if ((num_ids > 0 && !ids) || (num_blocks > 0 && !mask))
+    return fail(PKV_ERR_INVALID_ARGUMENT, "null input or output pointer");
+  return pkv::launch_mark_blocks(ids, num_ids, id_offset, num_blocks, mask, as_stream(stream));
+}
+
+int pkv_compact_block_tables(const int32_t* block_tables, const int32_t* seq_lens,
+                             const uint8_t* evicted, int32_t* tables_out, int32_t* lens_out,
+                             int32_t num_seqs, int32_t max_blocks_per_seq, int32_t block_size,
+                             int64_t num_blocks, void* stream) {
+  clear_error();
+  if (num_seqs < 0 || max_blocks_per_seq < 0 || block_size <= 0 || num_blocks < 0)
+    return fail(PKV_ERR_INVALID_ARGUMENT, "invalid table shape");
+  if (num_seqs > 0 && (!block_tables || !seq_lens || !evicted || !tables_out || !lens_out))
+    return fail(PKV_ERR_INVALID_ARGUMENT, "null input or output pointer");
+  return pkv::launch_compact_tables(block_tables, seq_lens, evicted, tables_out, lens_out,
+                                    num_seqs, max_blocks_per_seq, block_size, num_blocks,
+                                    as_stream(stream));
 }
 
 static int check_decode(const pkv::DecodeArgs& a) {

@@ -19,8 +19,18 @@ int* device_error_word();
 void set_error(const std::string& msg);
 
 // ---- quantize.cu ----------------------------------------------------------
+// skip (nullable): blocks with a nonzero byte are neither read nor written.
 int launch_quantize(const void* kv, int dtype, int8_t* q, float* scale, int64_t num_blocks,
-                    int block_size, int num_kv_heads, int head_dim, cudaStream_t stream);
+                    int block_size, int num_kv_heads, int head_dim, const uint8_t* skip,
+                    cudaStream_t stream);
+
+// ---- compose.cu -------------------------------------------------------------
+int launch_mark_blocks(const int64_t* ids, int64_t n, int64_t id_offset, int64_t num_blocks,
+                       uint8_t* mask, cudaStream_t stream);
+int launch_compact_tables(const int32_t* block_tables, const int32_t* seq_lens,
+                          const uint8_t* evicted, int32_t* tables_out, int32_t* lens_out,
+                          int num_seqs, int max_blocks_per_seq, int block_size,
+                          int64_t num_blocks, cudaStream_t stream);
 
 int launch_write_to_cache(const void* key, const void* value, int dtype, int8_t* kv_cache,
                           float* scale_cache, const int64_t* slot_mapping, int64_t num_tokens,

@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <string>
 
 #include "pkv_common.cuh"
@@ -38,6 +40,47 @@ __device__ __forceinline__ int quantize_one(float x, float scale) {
   return __float2int_rn(r);
 }
 
+// Four int8 codes packed little-endian, by exact division (the rare path of
+// quantize_word, kept out of line so the hot loops stay small).
+__device__ __noinline__ uint32_t quantize_word_exact(float x0, float x1, float x2, float x3,
+                                                     float scale) {
+  return (uint32_t)(quantize_one(x0, scale) & 255) |
+         ((uint32_t)(quantize_one(x1, scale) & 255) << 8) |
+         ((uint32_t)(quantize_one(x2, scale) & 255) << 16) |
+         ((uint32_t)(quantize_one(x3, scale) & 255) << 24);
+}
+
+// Four codes packed little-endian.  Fast path, for a head whose absmax is
+// finite and whose scale has a finite reciprocal rcp = 1/scale (rounded to
+// nearest): y = x * rcp differs from fl(x/scale) by at most
+// 1.5 * 2^-23 * |x/scale| <= 2^-15.5, because |x| <= absmax keeps
+// |x/scale| <= 127 * (1 + 2^-24).  Adding 1.5 * 2^23 rounds y to an integer
+// half-to-even and leaves it, two's complement, in the low mantissa bits;
+// y minus that integer is exact.  When every y lies farther than 2^-15 from
+// a half-integer, fl(x/scale) rounds to the same integers; otherwise (about
+// 2.4e-4 of words) the exact division decides.  |y| < 127.5, so the clamp
+// to [-127, 127] never binds.  Heads with a non-finite absmax, or a scale
+// below 2^-128 (reciprocal overflows), take the exact division.
+__device__ __forceinline__ uint32_t quantize_word(const float (&f)[4], float scale, float rcp,
+                                                  bool fast) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  if (fast) {
+    uint32_t b[4];
+    bool near = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float y = __fmul_rn(f[i], rcp);
+      const float z = __fadd_rn(y, kRound);
+      near |= fabsf(__fsub_rn(y, __fsub_rn(z, kRound))) >= 0.5f - 0x1p-15f;
+      b[i] = __float_as_uint(z);
+    }
+    if (!near)
+      return __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040),
+                         0x5410);
+  }
+  return quantize_word_exact(f[0], f[1], f[2], f[3], scale);
+}
+
 // Loads 16 bytes as VEC values of T and widens them to float.
 template <typename T, int VEC>
 __device__ __forceinline__ void load_vec(const T* p, float (&f)[VEC]) {
@@ -53,10 +96,11 @@ __device__ __forceinline__ void load_vec(const T* p, float (&f)[VEC]) {
 template <typename T, bool VECTOR>
 __global__ void __launch_bounds__(kQThreads)
     quantize_kernel(const T* __restrict__ kv, int8_t* __restrict__ q, float* __restrict__ scale,
-                    int bs, int hkv, int hd) {
+                    int bs, int hkv, int hd, const uint8_t* __restrict__ skip) {
   constexpr int VEC = 16 / sizeof(T);
   extern __shared__ uint32_t s_amax[];  // [hkv] float bits, then reused as scales
   const int64_t b = blockIdx.x;
+  if (skip != nullptr && skip[b]) return;  // whole CTA: block left untouched
   const int64_t elems = (int64_t)bs * hkv * hd;
   const T* src = kv + b * elems;
   int8_t* dst = q + b * elems;
@@ -147,11 +191,13 @@ __device__ __forceinline__ void load4<__nv_bfloat16>(const __nv_bfloat16* p, flo
 template <typename T, int BS>
 __global__ void __launch_bounds__(kQThreads)
     quantize_d128_kernel(const T* __restrict__ kv, int8_t* __restrict__ q,
-                         float* __restrict__ scale, int64_t units, int hkv) {
+                         float* __restrict__ scale, int64_t units, int hkv,
+                         const uint8_t* __restrict__ skip) {
   const int lane = threadIdx.x & 31;
   const int64_t unit = (int64_t)blockIdx.x * (kQThreads / 32) + (threadIdx.x >> 5);
   if (unit >= units) return;  // whole warp
   const int64_t b = unit / hkv;
+  if (skip != nullptr && skip[b]) return;  // whole warp: block left untouched
   const int h = (int)(unit - b * hkv);
   const int64_t tok_stride = (int64_t)hkv * 128;
   const int64_t base = (b * BS * hkv + h) * 128 + lane * 4;
@@ -167,38 +213,221 @@ __global__ void __launch_bounds__(kQThreads)
   const float amax = __uint_as_float(m);
   const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
   if (lane == 0) scale[unit] = s;
+  const float rcp = __frcp_rn(s);
+  const bool fast = isfinite(amax) && !isinf(rcp);
 #pragma unroll
   for (int t = 0; t < BS; ++t) {
-    const uint32_t w = (uint32_t)(quantize_one(v[t][0], s) & 255) |
-                       ((uint32_t)(quantize_one(v[t][1], s) & 255) << 8) |
-                       ((uint32_t)(quantize_one(v[t][2], s) & 255) << 16) |
-                       ((uint32_t)(quantize_one(v[t][3], s) & 255) << 24);
+    const uint32_t w = quantize_word(v[t], s, rcp, fast);
     *reinterpret_cast<uint32_t*>(q + base + t * tok_stride) = w;
   }
 }
 
+// head_dim 128, 16-token blocks of at most kBulkMaxBlock bytes (fp16/bf16
+// with <= 9 KV heads, fp32 with <= 4): a persistent kernel streams whole
+// blocks (contiguous in the [NB, bs, Hkv, D] layout) into a ring of shared
+// memory stages with one cp.async.bulk each.  Two groups of eight warps take
+// alternate blocks; in a group a warp quantizes one head from shared memory
+// (absmax pass, then codes).  Deep queues with few registers: the register
+// kernel above keeps one block-head in flight per warp and its CTAs turn
+// over every few microseconds.
+constexpr int kBulkGroups = 2;
+constexpr int kBulkGroupWarps = 8;
+constexpr int kBulkConsumerWarps = kBulkGroups * kBulkGroupWarps;
+constexpr int kBulkThreads = kBulkConsumerWarps * 32 + 32;
+constexpr uint32_t kBulkMaxBlock = 36 * 1024;
+constexpr int kBulkStages = 3;
+
+template <typename T>
+__device__ __forceinline__ void load4_shared(const T* p, float (&f)[4]) {
+  load4<T>(p, f);
+}
+
+// Bits of max |x| over a lane's four values of one row.  32-bit inputs: the
+// float bits with the sign cleared (unsigned order = magnitude order, NaN
+// above +inf).  16-bit inputs: |x| and a NaN-propagating max on the packed
+// pair; the surviving pair is widened once per head (absmax_float_bits).
+template <typename T>
+__device__ __forceinline__ uint32_t absmax_bits4(const T* p);
+template <>
+__device__ __forceinline__ uint32_t absmax_bits4<float>(const float* p) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  return max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+             max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu));
+}
+template <>
+__device__ __forceinline__ uint32_t absmax_bits4<__half>(const __half* p) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  const __half2 m = __hmax2_nan(__habs2(*reinterpret_cast<const __half2*>(&v.x)),
+                                __habs2(*reinterpret_cast<const __half2*>(&v.y)));
+  return *reinterpret_cast<const uint32_t*>(&m);
+}
+template <>
+__device__ __forceinline__ uint32_t absmax_bits4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162 m =
+      __hmax2_nan(__habs2(*reinterpret_cast<const __nv_bfloat162*>(&v.x)),
+                  __habs2(*reinterpret_cast<const __nv_bfloat162*>(&v.y)));
+  return *reinterpret_cast<const uint32_t*>(&m);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t absmax_fold(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t absmax_fold<float>(uint32_t a, uint32_t b) { return max(a, b); }
+template <>
+__device__ __forceinline__ uint32_t absmax_fold<__half>(uint32_t a, uint32_t b) {
+  const __half2 m = __hmax2_nan(*reinterpret_cast<const __half2*>(&a),
+                                *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&m);
+}
+template <>
+__device__ __forceinline__ uint32_t absmax_fold<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  const __nv_bfloat162 m = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                       *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&m);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t absmax_float_bits(uint32_t m);
+template <>
+__device__ __forceinline__ uint32_t absmax_float_bits<float>(uint32_t m) { return m; }
+template <>
+__device__ __forceinline__ uint32_t absmax_float_bits<__half>(uint32_t m) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&m));
+  return max(__float_as_uint(f.x) & 0x7fffffffu, __float_as_uint(f.y) & 0x7fffffffu);
+}
+template <>
+__device__ __forceinline__ uint32_t absmax_float_bits<__nv_bfloat16>(uint32_t m) {
+  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&m));
+  return max(__float_as_uint(f.x) & 0x7fffffffu, __float_as_uint(f.y) & 0x7fffffffu);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kBulkThreads, 2)
+    quantize_bulk_kernel(const T* __restrict__ kv, int8_t* __restrict__ q,
+                         float* __restrict__ scale, int64_t nb, int hkv,
+                         const uint8_t* __restrict__ skip, int* err) {
+  constexpr int BS = 16;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int64_t elems = (int64_t)BS * hkv * 128;
+  const uint32_t block_bytes = (uint32_t)(elems * sizeof(T));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kBulkStages * block_bytes);
+  uint64_t* empty = full + kBulkStages;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < kBulkStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kBulkGroupWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == kBulkConsumerWarps) {  // producer
+    if (lane == 0) {
+      int n = 0;
+      for (int64_t b = blockIdx.x; b < nb; b += gridDim.x) {
+        if (skip != nullptr && skip[b]) continue;
+        const int st = n % kBulkStages;
+        const uint32_t ph = (uint32_t)(n / kBulkStages) & 1u;
+        if (!mbar_wait_bounded(&empty[st], ph ^ 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          break;
+        }
+        mbar_arrive_expect_tx(&full[st], block_bytes);
+        bulk_load_g2s(smem_raw + st * block_bytes, kv + b * elems, block_bytes, &full[st]);
+        ++n;
+      }
+    }
+    return;
+  }
+
+  // block n of this CTA's sequence goes to group n % kBulkGroups
+  const int group = warp / kBulkGroupWarps;
+  const int gw = warp % kBulkGroupWarps;
+  bool live = true;
+  int n = 0;
+  for (int64_t b = blockIdx.x; b < nb; b += gridDim.x) {
+    if (skip != nullptr && skip[b]) continue;
+    const bool mine = n % kBulkGroups == group;
+    const int st = n % kBulkStages;
+    const uint32_t ph = (uint32_t)(n / kBulkStages) & 1u;
+    ++n;
+    if (!mine) continue;
+    if (live && !mbar_wait_bounded(&full[st], ph, err)) {
+      record_error(err, kDevWaitTimeout);
+      live = false;
+    }
+    if (live) {
+      const T* blk = reinterpret_cast<const T*>(smem_raw + st * block_bytes);
+      for (int h = gw; h < hkv; h += kBulkGroupWarps) {
+        const T* row0 = blk + (int64_t)h * 128 + lane * 4;
+        const int64_t tok = (int64_t)hkv * 128;
+        uint32_t m = absmax_bits4<T>(row0);
+#pragma unroll 5
+        for (int t = 1; t < BS; ++t) m = absmax_fold<T>(m, absmax_bits4<T>(row0 + t * tok));
+        m = __reduce_max_sync(0xffffffffu, absmax_float_bits<T>(m));  // NaN wins
+        const float amax = __uint_as_float(m);
+        const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+        if (lane == 0) scale[b * hkv + h] = s;
+        const float rcp = __frcp_rn(s);
+        const bool fast = isfinite(amax) && !isinf(rcp);
+        int8_t* out = q + b * elems + (int64_t)h * 128 + lane * 4;
+#pragma unroll 2
+        for (int t = 0; t < BS; ++t) {
+          float f[4];
+          load4_shared<T>(row0 + t * tok, f);
+          *reinterpret_cast<uint32_t*>(out + t * tok) = quantize_word(f, s, rcp, fast);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+}
+
+int sm_count_quant() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
 template <typename T>
 int launch_quantize_t(const T* kv, int8_t* q, float* scale, int64_t nb, int bs, int hkv, int hd,
-                      cudaStream_t stream) {
+                      const uint8_t* skip, cudaStream_t stream) {
   constexpr int VEC = 16 / sizeof(T);
+  const uint64_t block_bytes = (uint64_t)bs * hkv * hd * sizeof(T);
+  if (hd == 128 && bs == 16 && block_bytes <= kBulkMaxBlock &&
+      reinterpret_cast<uintptr_t>(kv) % 16 == 0 && reinterpret_cast<uintptr_t>(q) % 4 == 0 &&
+      std::getenv("PKV_QUANTIZE_REGISTER") == nullptr) {
+    const size_t smem = kBulkStages * block_bytes + 2 * kBulkStages * sizeof(uint64_t);
+    auto kern = quantize_bulk_kernel<T>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int64_t ctas = std::min<int64_t>(nb, 2LL * sm_count_quant());
+    kern<<<(unsigned)ctas, kBulkThreads, smem, stream>>>(kv, q, scale, nb, hkv, skip,
+                                                          device_error_word());
+    return kOk;
+  }
   if (hd == 128 && (bs == 16 || bs == 32) &&
       reinterpret_cast<uintptr_t>(kv) % (4 * sizeof(T)) == 0 &&
       reinterpret_cast<uintptr_t>(q) % 4 == 0) {
     const int64_t units = nb * hkv;
     const unsigned grid = (unsigned)((units + kQThreads / 32 - 1) / (kQThreads / 32));
     if (bs == 16)
-      quantize_d128_kernel<T, 16><<<grid, kQThreads, 0, stream>>>(kv, q, scale, units, hkv);
+      quantize_d128_kernel<T, 16><<<grid, kQThreads, 0, stream>>>(kv, q, scale, units, hkv, skip);
     else
-      quantize_d128_kernel<T, 32><<<grid, kQThreads, 0, stream>>>(kv, q, scale, units, hkv);
+      quantize_d128_kernel<T, 32><<<grid, kQThreads, 0, stream>>>(kv, q, scale, units, hkv, skip);
     return kOk;
   }
   const bool vec = hd % VEC == 0 && reinterpret_cast<uintptr_t>(kv) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(q) % VEC == 0;
   const size_t smem = (size_t)hkv * sizeof(uint32_t);
   if (vec)
-    quantize_kernel<T, true><<<(unsigned)nb, kQThreads, smem, stream>>>(kv, q, scale, bs, hkv, hd);
+    quantize_kernel<T, true><<<(unsigned)nb, kQThreads, smem, stream>>>(kv, q, scale, bs, hkv, hd,
+                                                                         skip);
   else
-    quantize_kernel<T, false><<<(unsigned)nb, kQThreads, smem, stream>>>(kv, q, scale, bs, hkv, hd);
+    quantize_kernel<T, false><<<(unsigned)nb, kQThreads, smem, stream>>>(kv, q, scale, bs, hkv, hd,
+                                                                          skip);
   return kOk;
 }
 
@@ -287,16 +516,17 @@ int launch_wtc_t(const T* key, const T* value, int8_t* kv_cache, float* scale_ca
 }  // namespace
 
 int launch_quantize(const void* kv, int dtype, int8_t* q, float* scale, int64_t num_blocks,
-                    int block_size, int num_kv_heads, int head_dim, cudaStream_t stream) {
+                    int block_size, int num_kv_heads, int head_dim, const uint8_t* skip,
+                    cudaStream_t stream) {
   if (num_blocks == 0) return kOk;
   int rc;
   switch (dtype) {
     case 0: rc = launch_quantize_t(static_cast<const float*>(kv), q, scale, num_blocks, block_size,
-                                   num_kv_heads, head_dim, stream); break;
+                                   num_kv_heads, head_dim, skip, stream); break;
     case 1: rc = launch_quantize_t(static_cast<const __half*>(kv), q, scale, num_blocks,
-                                   block_size, num_kv_heads, head_dim, stream); break;
+                                   block_size, num_kv_heads, head_dim, skip, stream); break;
     case 2: rc = launch_quantize_t(static_cast<const __nv_bfloat16*>(kv), q, scale, num_blocks,
-                                   block_size, num_kv_heads, head_dim, stream); break;
+                                   block_size, num_kv_heads, head_dim, skip, stream); break;
     default: set_error("unknown kv dtype code"); return kInvalidArgument;
   }
   if (rc != kOk) return rc;

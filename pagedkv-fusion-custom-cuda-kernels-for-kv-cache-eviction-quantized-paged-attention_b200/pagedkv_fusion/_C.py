@@ -49,6 +49,10 @@ _merge = _sig("pkv_eviction_merge", [_P, _I64, _I64, _P, _P, _SZ, _P])
 _quant = _sig("pkv_quantize_kv_per_block", [_P, _I32, _P, _P, _I64, _I32, _I32, _I32, _P])
 _attn_ws = _sig("pkv_quant_paged_attention_workspace_size", [_I32] * 6, _SZ)
 _attn_launches = _sig("pkv_quant_paged_attention_kernel_launches", [_I32] * 6, ct.c_int)
+_quant_except = _sig("pkv_quantize_kv_per_block_except",
+                     [_P, _I32, _P, _P, _P, _I64, _I32, _I32, _I32, _P])
+_mark = _sig("pkv_mark_blocks", [_P, _I64, _I64, _I64, _P, _P])
+_compact = _sig("pkv_compact_block_tables", [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _P])
 _attn = _sig("pkv_quant_paged_attention",
              [_P] * 8 + [_I32] * 5 + [_I64, _I32, _F, _P, _SZ, _P])
 _wtc_ws = _sig("pkv_write_to_cache_workspace_size", [_I64, _I32], _SZ)
@@ -208,6 +212,62 @@ def quantize_kv_per_block(kv, out_q=None, out_scale=None):
     _check(_quant(x.data_ptr(), _DTYPE_CODE[x.dtype], q.data_ptr(), scale.data_ptr(), nb, bs,
                   nkv, hd, _stream(x)))
     return q, scale
+
+
+def quantize_kv_per_block_except(kv, skip, out_q, out_scale):
+    """quantize_kv_per_block into ``out_q`` / ``out_scale`` for the blocks
+    whose ``skip`` byte is zero; blocks with a nonzero byte are left as they
+    are (the survivors of an eviction are quantized, the evicted ones not)."""
+    _require(kv.is_cuda and skip.is_cuda, "kv and skip must be CUDA tensors")
+    if kv.dim() != 4:
+        raise ValueError(f"expected 4D [nb, bs, nkv, hd], got {tuple(kv.shape)}")
+    _require(kv.dtype in _DTYPE_CODE, "kv must be float32, float16 or bfloat16")
+    x = kv.contiguous()
+    nb, bs, nkv, hd = x.shape
+    _require(skip.dtype in (torch.uint8, torch.bool) and skip.numel() == nb and skip.is_contiguous(),
+             "skip must be a contiguous uint8/bool [num_blocks] tensor")
+    _require(out_q.dtype == torch.int8 and tuple(out_q.shape) == tuple(x.shape)
+             and out_q.is_contiguous() and out_q.device == x.device,
+             "out_q must be a contiguous int8 tensor shaped like kv")
+    _require(out_scale.dtype == torch.float32 and tuple(out_scale.shape) == (nb, nkv)
+             and out_scale.is_contiguous() and out_scale.device == x.device,
+             "out_scale must be a contiguous float32 [num_blocks, num_kv_heads] tensor")
+    _check(_quant_except(x.data_ptr(), _DTYPE_CODE[x.dtype], skip.data_ptr(), out_q.data_ptr(),
+                         out_scale.data_ptr(), nb, bs, nkv, hd, _stream(x)))
+    return out_q, out_scale
+
+
+def mark_blocks(ids, id_offset: int, num_blocks: int):
+    """uint8 [num_blocks] mask with 1 at ``id - id_offset`` for each id of
+    ``ids`` (int64, global block ids) that falls in this range."""
+    _require(ids.is_cuda, "ids must be a CUDA tensor")
+    _require(ids.dtype == torch.int64 and ids.dim() == 1, "ids must be int64 [n]")
+    i = ids.contiguous()
+    mask = torch.empty(int(num_blocks), dtype=torch.uint8, device=i.device)
+    _check(_mark(i.data_ptr(), i.numel(), int(id_offset), int(num_blocks), mask.data_ptr(),
+                 _stream(i)))
+    return mask
+
+
+def compact_block_tables(block_tables, seq_lens, evicted, num_blocks: int, block_size: int):
+    """Block tables without the evicted blocks and the tokens each sequence
+    keeps: ``(tables, lens)``, int32, a valid input to quant_paged_attention."""
+    _require(block_tables.is_cuda and seq_lens.is_cuda and evicted.is_cuda,
+             "all inputs must be CUDA tensors")
+    _require(block_tables.dtype == torch.int32 and block_tables.dim() == 2,
+             "block_tables must be int32 [S, M]")
+    _require(evicted.dtype in (torch.uint8, torch.bool) and evicted.numel() == int(num_blocks),
+             "evicted must be a uint8/bool [num_blocks] mask")
+    bt = block_tables.contiguous()
+    S, M = bt.shape
+    sl = seq_lens.to(torch.int32).contiguous()
+    _require(sl.numel() == S, "seq_lens must have num_seqs entries")
+    ev = evicted.contiguous()
+    out_bt = torch.empty_like(bt)
+    out_sl = torch.empty_like(sl)
+    _check(_compact(bt.data_ptr(), sl.data_ptr(), ev.data_ptr(), out_bt.data_ptr(),
+                    out_sl.data_ptr(), S, M, int(block_size), int(num_blocks), _stream(bt)))
+    return out_bt, out_sl
 
 
 def eviction_select(scores, k: int):

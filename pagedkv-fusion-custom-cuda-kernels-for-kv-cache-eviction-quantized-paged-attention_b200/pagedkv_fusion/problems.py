@@ -14,6 +14,10 @@ The ``workload_*`` helpers build the named benchmark workloads:
                            entries x10 before quantization
 * decode large-head     -- 512 seqs, L ~ U[1024, 8192] (multiple of 16),
                            40/40 heads, ~147K blocks (~24 GB INT8 KV)
+* evict -> quantize -> decode composition -- 1,024 seqs, L ~ U[4096, 32768]
+                           (multiple of 16), 8/8 heads, fp16 K/V, 15 % of
+                           the blocks evicted (``composition_seq_lens``;
+                           ``composition_problem`` builds small instances)
 """
 
 from __future__ import annotations
@@ -28,6 +32,8 @@ __all__ = [
     "eviction_problem",
     "decode_heavy_tail_problem",
     "large_head_seq_lens",
+    "composition_seq_lens",
+    "composition_problem",
     "balanced_shards",
 ]
 
@@ -127,6 +133,44 @@ def large_head_seq_lens(seed: int = 0, num_seqs: int = 512, lo: int = 1024,
     raw = rng.uniform(lo, hi, size=num_seqs)
     lens = (np.rint(raw / block_size) * block_size).astype(np.int64)
     return np.clip(lens, lo, hi).astype(np.int32)
+
+
+def composition_seq_lens(seed: int = 0, num_seqs: int = 1024, lo: int = 4096,
+                         hi: int = 32768, block_size: int = 16) -> np.ndarray:
+    """Sequence lengths uniform in [lo, hi], rounded to multiples of 16."""
+    return large_head_seq_lens(seed, num_seqs, lo, hi, block_size)
+
+
+def composition_problem(seed: int = 0, num_seqs: int = 6, lo: int = 1, hi: int = 300,
+                        heads: int = 8, kv_heads: int = 8, head_dim: int = 128,
+                        block_size: int = 16, spare_blocks: int = 5):
+    """A small instance of the evict -> quantize -> decode step.
+
+    Ragged lengths in [lo, hi] (a partial last page is common), a shuffled
+    block order with ``spare_blocks`` never-referenced blocks, fp16 K/V
+    ~N(0,1) and the eviction statistics of ``eviction_problem``.  Returns
+    ``(q, k, v, recency, frequency, attn, valid, block_tables, seq_lens,
+    sm_scale)``; K/V are float16 numpy arrays.
+    """
+    rng = np.random.default_rng(seed)
+    seq_lens = rng.integers(lo, hi + 1, size=num_seqs).astype(np.int32)
+    pages = (seq_lens + block_size - 1) // block_size
+    nb = int(pages.sum()) + spare_blocks
+    perm = rng.permutation(nb).astype(np.int32)
+    tables = np.full((num_seqs, int(pages.max())), -1, dtype=np.int32)
+    starts = np.concatenate([[0], np.cumsum(pages)])
+    for s_ in range(num_seqs):
+        tables[s_, :pages[s_]] = perm[starts[s_]:starts[s_ + 1]]
+    shape = (nb, block_size, kv_heads, head_dim)
+    k = rng.standard_normal(shape, dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal(shape, dtype=np.float32).astype(np.float16)
+    q = rng.standard_normal((num_seqs, heads, head_dim), dtype=np.float32)
+    recency = rng.random(nb, dtype=np.float32)
+    frequency = rng.random(nb, dtype=np.float32)
+    attn = rng.random((nb, block_size), dtype=np.float32)
+    valid = rng.random((nb, block_size)) > 0.2
+    return (q, k, v, recency, frequency, attn, valid, tables, seq_lens,
+            1.0 / math.sqrt(head_dim))
 
 
 def balanced_shards(seq_lens, world_size: int) -> list[np.ndarray]:

@@ -84,3 +84,66 @@ def test_two_gpus_sharded_eviction_and_decode():
         assert r[1] != "crash", r[2]
         assert r[1] is True, f"rank {r[0]}: sharded eviction differs from the oracle"
         assert r[2] <= 1e-3, f"rank {r[0]}: decode max rel error {r[2]}"
+
+
+def _compose_worker(rank, world, port, q):
+    try:
+        for p in (str(PKG), str(ROOT)):
+            sys.path.insert(0, p)
+        import torch.distributed as dist
+        from oracle import c_oracle
+        from oracle import oracle as O
+        from pagedkv_fusion import problems
+        from pagedkv_fusion.compose import evict_quantize_decode
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        # rank r owns an independent problem; global block ids concatenate
+        # the ranks' blocks in rank order
+        probs = [problems.composition_problem(30 + r, num_seqs=20, lo=1, hi=800)
+                 for r in range(world)]
+        sizes = [p[1].shape[0] for p in probs]
+        offsets = np.concatenate([[0], np.cumsum(sizes)])
+        total = int(offsets[-1])
+        n_ev = int(0.15 * total)
+        (qh, k, v, rec, freq, att, val, bt, sl, sm) = probs[rank]
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        out, ids, tables, lens = evict_quantize_decode(
+            d(qh), d(k), d(v), d(rec), d(freq), d(att), d(val), d(bt), d(sl), n_ev, sm,
+            block_offset=int(offsets[rank]), total_blocks=total)
+        scores = np.concatenate([O.eviction_scores(*p[3:7]) for p in probs])
+        want_ids = O.select_eviction_candidates(scores, n_ev)
+        ids_ok = bool(np.array_equal(ids.cpu().numpy(), want_ids))
+        mask = O.mark_blocks(want_ids, int(offsets[rank]), sizes[rank])
+        want_t, want_l = O.compact_block_tables(bt, sl, mask, k.shape[1])
+        tab_ok = bool(np.array_equal(tables.cpu().numpy(), want_t)
+                      and np.array_equal(lens.cpu().numpy(), want_l))
+        kq, ks = O.quantize_kv_per_block(k.astype(np.float32))
+        vq, vs = O.quantize_kv_per_block(v.astype(np.float32))
+        want = c_oracle.paged_attention(qh, kq, ks, vq, vs, want_t, want_l, sm)
+        got = out.cpu().numpy()
+        err = float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, ids_ok and tab_ok, err))
+    except Exception:
+        q.put((rank, "crash", traceback.format_exc()))
+
+
+def test_two_gpus_evict_quantize_decode():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_compose_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=300) for _ in procs), key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert r[1] != "crash", r[2]
+        assert r[1] is True, f"rank {r[0]}: evicted ids or compacted tables differ"
+        assert r[2] <= 1e-3, f"rank {r[0]}: decode max rel error {r[2]}"
