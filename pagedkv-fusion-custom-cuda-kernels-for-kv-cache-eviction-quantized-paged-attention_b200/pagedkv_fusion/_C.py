@@ -15,6 +15,7 @@ this module fails with ``ImportError`` when that library has not been built.
 from __future__ import annotations
 
 import ctypes as ct
+import os
 from pathlib import Path
 
 import torch
@@ -61,6 +62,10 @@ _wtc = _sig("pkv_write_to_cache",
 
 LIBRARY_PATH = str(_LIB_PATH)
 _DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+_FUSED_WS_CACHE: dict = {}  # (num_blocks, k, device, env) -> workspace bytes
+_SELECT_WS_CACHE: dict = {}
 
 
 def _check(rc: int):
@@ -285,7 +290,10 @@ def eviction_select(scores, k: int):
     out = torch.empty(kk, dtype=torch.int64, device=s.device)
     if kk == 0:
         return out
-    nbytes = _select_ws(n, kk)
+    key = (n, kk, s.device.index, os.environ.get("PKV_EVICTION_MULTI_KERNEL"))
+    nbytes = _SELECT_WS_CACHE.get(key)
+    if nbytes is None:
+        nbytes = _SELECT_WS_CACHE[key] = _select_ws(n, kk)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=s.device) if nbytes else None
     rc = _select(s.data_ptr(), n, kk, out.data_ptr(), 0 if ws is None else ws.data_ptr(),
                  nbytes, torch._C._cuda_getCurrentRawStream(s.device.index))
@@ -296,26 +304,48 @@ def eviction_select(scores, k: int):
 
 def eviction_scores_select(recency, frequency, attn_weights, valid_mask, k: int,
                            w_recency=0.4, w_frequency=0.3, w_attention=0.3):
-    """Scores and the k selected block ids from one call: ``(scores, idx)``."""
-    _require(recency.is_cuda and frequency.is_cuda and attn_weights.is_cuda and valid_mask.is_cuda,
-             "all inputs must be CUDA tensors")
-    _require(recency.dtype == torch.float32 and frequency.dtype == torch.float32
-             and attn_weights.dtype == torch.float32, "recency/frequency/attn must be float32")
-    _require(attn_weights.dim() == 2, "attn_weights must be [num_blocks, block_size]")
-    _require(valid_mask.dtype == torch.bool, "valid_mask must be bool")
+    """Scores and the k selected block ids from one call: ``(scores, idx)``.
+
+    Checks are plain attribute tests and the workspace size is cached per
+    (num_blocks, k, device, forced multi-kernel path): this call sits on the
+    eviction latency path, where a few microseconds of Python are a large
+    share of the total.
+    """
+    if not (recency.is_cuda and frequency.is_cuda and attn_weights.is_cuda
+            and valid_mask.is_cuda):
+        raise RuntimeError("all inputs must be CUDA tensors")
+    if recency.dtype is not _F32 or frequency.dtype is not _F32 or attn_weights.dtype is not _F32:
+        raise RuntimeError("recency/frequency/attn must be float32")
+    if attn_weights.dim() != 2:
+        raise RuntimeError("attn_weights must be [num_blocks, block_size]")
+    if valid_mask.dtype is not _BOOL:
+        raise RuntimeError("valid_mask must be bool")
     k = int(k)
-    _require(k >= 0, "k must be non-negative")
+    if k < 0:
+        raise RuntimeError("k must be non-negative")
     nb, bs = attn_weights.shape
-    _require(tuple(valid_mask.shape) == (nb, bs), "valid_mask must match attn_weights")
-    rec, freq = recency.contiguous(), frequency.contiguous()
-    att, msk = attn_weights.contiguous(), valid_mask.contiguous()
-    scores = torch.empty(nb, dtype=torch.float32, device=rec.device)
-    kk = min(k, nb)
-    idx = torch.empty(kk, dtype=torch.int64, device=rec.device)
-    ws, wp = _workspace(_fused_ws(nb, kk) if kk else 0, rec.device)
-    _check(_fused(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
-                  scores.data_ptr(), nb, bs, w_recency, w_frequency, w_attention, kk,
-                  idx.data_ptr(), wp, 0 if ws is None else ws.numel(), _stream(rec)))
+    if valid_mask.shape != attn_weights.shape:
+        raise RuntimeError("valid_mask must match attn_weights")
+    rec = recency if recency.is_contiguous() else recency.contiguous()
+    freq = frequency if frequency.is_contiguous() else frequency.contiguous()
+    att = attn_weights if attn_weights.is_contiguous() else attn_weights.contiguous()
+    msk = valid_mask if valid_mask.is_contiguous() else valid_mask.contiguous()
+    dev = rec.device
+    scores = torch.empty(nb, dtype=_F32, device=dev)
+    kk = k if k < nb else nb
+    idx = torch.empty(kk, dtype=torch.int64, device=dev)
+    key = (nb, kk, dev.index, os.environ.get("PKV_EVICTION_MULTI_KERNEL"))
+    nbytes = _FUSED_WS_CACHE.get(key)
+    if nbytes is None:
+        nbytes = _fused_ws(nb, kk) if kk else 0
+        _FUSED_WS_CACHE[key] = nbytes
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
+    rc = _fused(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
+                scores.data_ptr(), nb, bs, w_recency, w_frequency, w_attention, kk,
+                idx.data_ptr(), None if ws is None else ws.data_ptr(), nbytes,
+                torch._C._cuda_getCurrentRawStream(dev.index))
+    if rc:
+        _check(rc)
     return scores, idx
 
 

@@ -35,6 +35,7 @@ __all__ = [
     "eviction_scores",
     "select_eviction_candidates",
     "eviction_scores_and_candidates",
+    "EvictionPlan",
     "quant_paged_attention",
 ]
 
@@ -151,6 +152,41 @@ def eviction_scores_and_candidates(recency, frequency, attn_weights, valid_mask,
                                            st.to_device(valid_mask, torch.bool), int(k),
                                            w_recency, w_frequency, w_attention)
     return st.back(scores), st.back(idx)
+
+
+class EvictionPlan:
+    """``eviction_scores_and_candidates`` captured once as a CUDA graph over
+    fixed statistics buffers, for a serving loop that updates
+    ``recency`` / ``frequency`` / ``attn_weights`` / ``valid_mask`` in place
+    each step and then calls :meth:`run`.  A replay skips the per-call
+    argument checks, allocations and launch of the eager call; the results
+    land in the same ``scores`` / ``indices`` tensors every time.
+
+    The buffers must be CUDA tensors that stay alive (and keep their
+    storage) while the plan is used.
+    """
+
+    def __init__(self, recency, frequency, attn_weights, valid_mask, k: int,
+                 w_recency: float = 0.4, w_frequency: float = 0.3, w_attention: float = 0.3):
+        C = _lib()
+        if not _all_cuda(recency, frequency, attn_weights, valid_mask):
+            raise RuntimeError("EvictionPlan needs CUDA tensors (it binds their storage)")
+        self._inputs = (recency, frequency, attn_weights, valid_mask)
+        args = (recency, frequency, attn_weights, valid_mask, int(k), w_recency, w_frequency,
+                w_attention)
+        side = torch.cuda.Stream(device=recency.device)
+        side.wait_stream(torch.cuda.current_stream(recency.device))
+        with torch.cuda.stream(side):
+            C.eviction_scores_select(*args)  # first call: cluster set-up, workspace sizes
+        torch.cuda.current_stream(recency.device).wait_stream(side)
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph):
+            self.scores, self.indices = C.eviction_scores_select(*args)
+
+    def run(self):
+        """Replays the capture on the current stream; returns ``(scores, indices)``."""
+        self._graph.replay()
+        return self.scores, self.indices
 
 
 # ---------------------------------------------------------------------------

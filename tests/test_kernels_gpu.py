@@ -474,3 +474,20 @@ def test_write_to_cache_matches_oracle(cuda):
     cuda.write_to_cache(dev(key), dev(val), dc, ds, dev(slots), bs)
     np.testing.assert_array_equal(dc.cpu().numpy(), want_c)
     np.testing.assert_array_equal(bits(ds), bits(want_s))
+
+
+def test_eviction_plan_replays_match_eager(cuda):
+    """The captured score + select replays on updated statistics buffers and
+    returns what the eager call returns for the same values."""
+    from pagedkv_fusion import ops
+    rec, freq, att, msk = problems.eviction_problem(seed=3)
+    d = [dev(a) for a in (rec, freq, att, msk)]
+    plan = ops.EvictionPlan(*d, 2458)
+    for seed in (3, 4, 5):
+        new = problems.eviction_problem(seed=seed, mask="random")
+        for buf, a in zip(d, new):
+            buf.copy_(dev(a))
+        scores, idx = plan.run()
+        want = O.select_eviction_candidates(O.eviction_scores(*new), 2458)
+        assert np.array_equal(idx.cpu().numpy(), want)
+        assert np.array_equal(bits(scores), bits(O.eviction_scores(*new)))
