@@ -208,9 +208,10 @@ int pkv_quant_paged_attention(const float *q, const int8_t *k_cache,
  * Number of kernels one pkv_quant_paged_attention call with these shapes
  * launches on its stream (16-byte aligned pointers): 1 for the persistent
  * stream kernel (up to 1,024 sequences with head_dim 128, block_size 16 or
- * 32 and a power-of-two GQA group <= 8), 2 for the split-K kernel and its
- * combine.  Lets a caller account for launches without a profiler.  No
- * counterpart in the reference.
+ * 32 and a GQA group of 1, or 2/4/8 at block_size 32), 2 for the
+ * tensor-core GQA kernel (block_size 16, groups of 2/4/8) or the split-K
+ * kernel, each with its combine.  Lets a caller account for launches
+ * without a profiler.  No counterpart in the reference.
  */
 int pkv_quant_paged_attention_kernel_launches(int32_t num_seqs, int32_t num_heads,
                                               int32_t num_kv_heads, int32_t head_dim,

@@ -1466,11 +1466,344 @@ __global__ void __launch_bounds__(128)
 }
 
 // ===========================================================================
+// Tensor-core kernel for GQA groups (tcgen05, int8, accumulators in TMEM)
+// ===========================================================================
+//
+// With G = 2..8 query heads per KV head the CUDA-core kernels spend G x 12
+// dp4a and G x 3 shared-memory digit loads per 16 bytes of K, and fall to
+// ~1 TB/s.  Here one CTA owns (sequence, KV head, split of <= 512 tokens)
+// and the products run on the tensor cores:
+//
+//   q.K  D1[t, n] = sum_d K[t, d] * Qd[n, d]   M = 128 tokens (8 pages), N = G x 3
+//        query digit planes (padded to 8/16/32), K-major A (the TMA page
+//        rows) and B (the digit planes), s8 x s8 -> s32 in TMEM;
+//   p.V  D2[d, n] = sum_t V[t, d] * Pd[n, t]   M = 128 channels, N = G x 3
+//        probability planes, A = the V page rows read MN-major, B = the
+//        planes written K-major by the softmax warps, s8 x u8 -> s32.
+//
+// The integer formats are the CUDA-core path's (query as three signed
+// base-256 digits of a 24-bit integer, p * v_scale as a 24-bit fixed point
+// relative to the split's largest V scale), so results match it to fp32
+// rounding.  Warp 0 issues the TMA page loads (one (128, 1, 16) box per
+// page: one head, so a tile is 128 consecutive 128-byte rows), warp 1 owns
+// tensor memory and issues the MMAs, warps 4-7 (one per 32-lane TMEM
+// quarter) turn logits into probabilities and read the results; partials
+// go through decode_combine_kernel.
+
+template <int G>
+struct TcCfg {
+  static constexpr int kNQ = G * 3 <= 8 ? 8 : (G * 3 <= 16 ? 16 : 32);  // MMA N
+  static constexpr int kTileTok = 128;
+  static constexpr int kPagesPerTile = 8;
+  static constexpr int kMaxTiles = 4;
+  static constexpr int kMaxTok = kMaxTiles * kTileTok;
+  static constexpr int kMaxPages = kMaxTiles * kPagesPerTile;
+  static constexpr int kStages = 4;
+  static constexpr int kThreads = 256;
+  static constexpr int kRowBytes = ((kNQ * 128 + 1023) / 1024) * 1024;  // one operand tile
+  static constexpr int kOffQ = kStages * kStageBytes;
+  static constexpr int kOffP = kOffQ + kRowBytes;
+  static constexpr int kOffLogit = kOffP + kMaxTiles * kRowBytes;
+  static constexpr int kOffPhys = kOffLogit + G * kMaxTok * 4;
+  static constexpr int kOffKs = kOffPhys + kMaxPages * 4;
+  static constexpr int kOffVs = kOffKs + kMaxPages * 4;
+  static constexpr int kOffQs = kOffVs + kMaxPages * 4;
+  static constexpr int kOffRed = kOffQs + 32;
+  static constexpr int kOffTmem = kOffRed + 2 * 4 * 8 * 4;
+  static constexpr int kOffBar = kOffTmem + 16;
+  static constexpr int kNumBars = 2 * kStages + 3;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 1024;
+  // D1: one kNQ-column slice per K tile, then D2
+  static constexpr int kD2Col = kMaxTiles * kNQ;
+  static constexpr int kTmemCols = (kD2Col + kNQ) <= 64 ? 64 : ((kD2Col + kNQ) <= 128 ? 128 : 256);
+  static_assert(2 * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs per SM");
+  static_assert(3 * kTmemCols <= 512 || 3 * (kSmemBytes + 1024) > 228 * 1024,
+                "CTAs that fit on an SM must fit in its tensor memory");
+};
+
+template <int G>
+__global__ void __launch_bounds__(256, 2)
+    decode_tc_kernel(const __grid_constant__ CUtensorMap map_k,
+                     const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q,
+                     const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+                     const int32_t* __restrict__ block_tables, const int32_t* __restrict__ seq_lens,
+                     float* __restrict__ out, float* __restrict__ ws_acc,
+                     float2* __restrict__ ws_ml, int num_heads, int num_kv_heads,
+                     int64_t num_blocks, int max_blocks_per_seq, float qk_scale,
+                     int pages_per_split, int max_splits, int* err) {
+  using C = TcCfg<G>;
+  constexpr int NQ = C::kNQ;
+  constexpr int BS = 16;
+  const int seq = blockIdx.x, split = blockIdx.y, j = blockIdx.z;
+  const int L = max(seq_lens[seq], 0);
+  const int n_pages = covered_pages(L, BS, max_blocks_per_seq);
+  if (split == 0 && j == 0 && threadIdx.x == 0 && L > n_pages * BS) record_error(err, kDevSeqTooLong);
+  const int n_splits = (n_pages + pages_per_split - 1) / pages_per_split;
+  if (split >= n_splits) return;  // uniform, before any barrier or TMEM use
+  const int p0 = split * pages_per_split;
+  const int np = min(pages_per_split, n_pages - p0);
+  const int T = min(L, (p0 + np) * BS) - p0 * BS;
+  const int n_tiles = (np + C::kPagesPerTile - 1) / C::kPagesPerTile;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* s_q = smem + C::kOffQ;
+  uint8_t* s_p = smem + C::kOffP;
+  float* s_logit = reinterpret_cast<float*>(smem + C::kOffLogit);
+  int* s_phys = reinterpret_cast<int*>(smem + C::kOffPhys);
+  float* s_ks = reinterpret_cast<float*>(smem + C::kOffKs);
+  float* s_vs = reinterpret_cast<float*>(smem + C::kOffVs);
+  float* s_qs = reinterpret_cast<float*>(smem + C::kOffQs);
+  float* s_red = reinterpret_cast<float*>(smem + C::kOffRed);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffTmem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* k_done = empty + C::kStages;
+  uint64_t* p_ready = k_done + 1;
+  uint64_t* pv_done = p_ready + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(k_done, 1);
+    mbar_init(p_ready, 1);
+    mbar_init(pv_done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(s_tmem, C::kTmemCols);
+  if (warp == 2 || warp == 3) {  // the split's block ids and scales
+    for (int pg = tid - 64; pg < np; pg += 64) {
+      const int phys = block_tables[(int64_t)seq * max_blocks_per_seq + p0 + pg];
+      const bool ok = phys >= 0 && (int64_t)phys < num_blocks;
+      if (!ok) record_error(err, kDevBadBlockId);
+      s_phys[pg] = ok ? phys : -1;
+      const int64_t si = (int64_t)(ok ? phys : 0) * num_kv_heads + j;
+      s_ks[pg] = ok ? k_scale[si] : 0.0f;
+      s_vs[pg] = ok ? v_scale[si] : 0.0f;
+    }
+  }
+  if (warp >= 4) {  // query digit planes: row 3g + plane of the B operand
+    const int w4 = warp - 4;
+    for (int g = w4; g < G; g += 4) {
+      const float4 x = reinterpret_cast<const float4*>(
+          q + ((int64_t)seq * num_heads + (int64_t)j * G + g) * 128)[lane];
+      float m = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+      m = warp_max(m);
+      const float inv = m > 0.0f ? (float)kQFix / m : 0.0f;
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+      int d[4][3];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int n = __float2int_rn(xs[e] * inv);
+        n = max(-kQFix, min(kQFix, n));
+        to_digits(n, d[e][0], d[e][1], d[e][2]);
+      }
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl)
+        *reinterpret_cast<uint32_t*>(s_q + sw128_offset(3 * g + pl, 4 * lane)) =
+            pack4(d[0][pl], d[1][pl], d[2][pl], d[3][pl]);
+      if (lane == 0) s_qs[g] = m > 0.0f ? m / (float)kQFix : 0.0f;
+    }
+    for (int r = 3 * G + w4; r < NQ; r += 4)  // padding rows
+      *reinterpret_cast<uint32_t*>(s_q + sw128_offset(r, 4 * lane)) = 0u;
+  }
+  fence_proxy_async_smem();
+  tmem_fence_before_sync();
+  __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    // ---- TMA: K tiles of the split, then its V tiles -------------------------
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+      int ns = 0;
+      bool ok_run = true;
+      for (int kind = 0; kind < 2 && ok_run; ++kind) {
+        for (int ti = 0; ti < n_tiles; ++ti, ++ns) {
+          const int st = ns % C::kStages;
+          const uint32_t ph = (uint32_t)(ns / C::kStages) & 1u;
+          if (!mbar_wait_bounded(&empty[st], ph ^ 1u, err)) {
+            record_error(err, kDevWaitTimeout);
+            ok_run = false;
+            break;
+          }
+          const int pb = ti * C::kPagesPerTile;
+          const int pe = min(np, pb + C::kPagesPerTile);
+          mbar_arrive_expect_tx(&full[st], (uint32_t)((pe - pb) * BS * 128));
+          for (int pg = pb; pg < pe; ++pg)
+            tma_load_3d(smem + st * kStageBytes + (pg - pb) * BS * 128, kind ? &map_v : &map_k,
+                        &full[st], 0, j, max(s_phys[pg], 0) * BS, policy);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issue: one thread ---------------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t kIdQK = umma_i8_idesc(1, 1, 0, 0, 128, NQ);
+      constexpr uint32_t kIdPV = umma_i8_idesc(1, 0, 1, 0, 128, NQ);
+      const uint32_t stage0 = smem_u32(smem);
+      const uint32_t qaddr = smem_u32(s_q);
+      const uint32_t paddr = smem_u32(s_p);
+      int ns = 0;
+      bool ok_run = true;
+      for (int ti = 0; ti < n_tiles && ok_run; ++ti, ++ns) {
+        const int st = ns % C::kStages;
+        if (!mbar_wait_bounded(&full[st], (uint32_t)(ns / C::kStages) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok_run = false;
+          break;
+        }
+        tmem_fence_after_sync();
+        const uint32_t a = stage0 + st * kStageBytes;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_i8(tmem + ti * NQ, umma_sw128_desc(a + k * 32, 16, 1024),
+                  umma_sw128_desc(qaddr + k * 32, 16, 1024), kIdQK, k > 0);
+        // frees the stage once these MMAs complete -- only when a later tile of
+        // this CTA reuses it: an arrival nobody waits for could land after the
+        // CTA has exited, in shared memory that belongs to the next CTA
+        if (ns + C::kStages < 2 * n_tiles) umma_commit(&empty[st]);
+      }
+      umma_commit(k_done);
+      if (ok_run && !mbar_wait_bounded(p_ready, 0, err)) {
+        record_error(err, kDevWaitTimeout);
+        ok_run = false;
+      }
+      tmem_fence_after_sync();
+      for (int ti = 0; ti < n_tiles && ok_run; ++ti, ++ns) {
+        const int st = ns % C::kStages;
+        if (!mbar_wait_bounded(&full[st], (uint32_t)(ns / C::kStages) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok_run = false;
+          break;
+        }
+        tmem_fence_after_sync();
+        const uint32_t a = stage0 + st * kStageBytes;
+        const uint32_t b = paddr + ti * C::kRowBytes;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_i8(tmem + C::kD2Col, umma_sw128_desc(a + k * 4096, 16, 1024),
+                  umma_sw128_desc(b + k * 32, 16, 1024), kIdPV, (ti > 0 || k > 0) ? 1u : 0u);
+        if (ns + C::kStages < 2 * n_tiles) umma_commit(&empty[st]);
+      }
+      umma_commit(pv_done);  // the last arrival: the epilogue waits for it
+    }
+  } else if (warp >= 4) {
+    // ---- logits, softmax, probability planes, output -----------------------
+    const int w4 = warp - 4;
+    const int e = tid - 128;  // TMEM lane: token of a tile, then channel
+    const uint32_t lane_base = (uint32_t)(32 * w4) << 16;
+    bool live = mbar_wait_bounded(k_done, 0, err);
+    if (!live) record_error(err, kDevWaitTimeout);
+    tmem_fence_after_sync();
+    float kmax[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) kmax[g] = -INFINITY;
+    for (int ti = 0; ti < n_tiles; ++ti) {
+      uint32_t r[NQ];
+      tmem_load<NQ>(tmem + lane_base + ti * NQ, r);
+      tmem_wait_load();
+      const int tok = ti * C::kTileTok + e;
+      const int pg = min(tok / BS, C::kMaxPages - 1);
+      const bool valid = live && tok < T && s_phys[pg] >= 0;
+      const float ks = s_ks[pg];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float v = (float)(int)r[3 * g + 2] * 65536.0f +
+                        ((float)(int)r[3 * g + 1] * 256.0f + (float)(int)r[3 * g]);
+        const float logit = valid ? v * (s_qs[g] * ks * qk_scale) : -INFINITY;
+        s_logit[g * C::kMaxTok + tok] = logit;
+        kmax[g] = fmaxf(kmax[g], logit);
+      }
+    }
+    float* red_m = s_red;
+    float* red_l = s_red + 32;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float m = warp_max(kmax[g]);
+      if (lane == 0) red_m[w4 * 8 + g] = m;
+    }
+    float vmax = 0.0f;
+    for (int pg = 0; pg < np; ++pg) vmax = fmaxf(vmax, s_vs[pg]);
+    const float to_fix = vmax > 0.0f ? 16777215.0f / vmax : 0.0f;
+    named_barrier(1, 128);
+    float m[G], l[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m[g] = fmaxf(fmaxf(red_m[g], red_m[8 + g]), fmaxf(red_m[16 + g], red_m[24 + g]));
+      l[g] = 0.0f;
+    }
+    for (int ti = 0; ti < n_tiles; ++ti) {
+      const int tok = ti * C::kTileTok + e;
+      const float vs = s_vs[min(tok / BS, C::kMaxPages - 1)];
+      uint8_t* pt = s_p + ti * C::kRowBytes;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        uint32_t n = 0;
+        if (tok < T && m[g] != -INFINITY) {
+          const float p = exp2f(s_logit[g * C::kMaxTok + tok] - m[g]);
+          l[g] += p;
+          n = __float2uint_rn(fminf(p * vs * to_fix, 16777215.0f));
+        }
+        pt[sw128_offset(3 * g, e)] = (uint8_t)(n & 255u);
+        pt[sw128_offset(3 * g + 1, e)] = (uint8_t)((n >> 8) & 255u);
+        pt[sw128_offset(3 * g + 2, e)] = (uint8_t)(n >> 16);
+      }
+      for (int rw = 3 * G; rw < NQ; ++rw) pt[sw128_offset(rw, e)] = 0;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float s = warp_sum(l[g]);
+      if (lane == 0) red_l[w4 * 8 + g] = s;
+    }
+    fence_proxy_async_smem();
+    named_barrier(1, 128);
+    if (e == 0) mbar_arrive(p_ready);
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      l[g] = (red_l[g] + red_l[8 + g]) + (red_l[16 + g] + red_l[24 + g]);
+    if (live && !mbar_wait_bounded(pv_done, 0, err)) {
+      record_error(err, kDevWaitTimeout);
+      live = false;
+    }
+    tmem_fence_after_sync();
+    uint32_t r[NQ];
+    tmem_load<NQ>(tmem + lane_base + C::kD2Col, r);
+    tmem_wait_load();
+    const float back = vmax * (1.0f / 16777215.0f);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float acc = ((float)(int)r[3 * g + 2] * 65536.0f +
+                         ((float)(int)r[3 * g + 1] * 256.0f + (float)(int)r[3 * g])) * back;
+      const int hq = j * G + g;
+      if (n_splits == 1) {
+        out[((int64_t)seq * num_heads + hq) * 128 + e] = l[g] > 0.0f ? acc / l[g] : 0.0f;
+      } else {
+        const int64_t slot = ((int64_t)seq * max_splits + split) * num_heads + hq;
+        ws_acc[slot * 128 + e] = acc;
+        if (e == 0) ws_ml[slot] = make_float2(m[g], l[g]);
+      }
+    }
+  }
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// ===========================================================================
 // Planning and dispatch
 // ===========================================================================
 
 struct Plan {
   bool fast = false;
+  bool tc = false;      // tensor-core GQA kernel (bs 16, group 2/4/8)
   bool stream = false;  // persistent balanced kernel (fast shapes, S <= 1024)
   int hg = 1, g = 1;
   int pages_per_split = 1;
@@ -1535,6 +1868,20 @@ Plan make_plan(const DecodeArgs& a) {
     int pps = max_pages;
     while (pps > 1 && (int64_t)a.num_seqs * a.num_heads * ((M + pps - 1) / pps) < 888) pps /= 2;
     p.pages_per_split = pps;
+  }
+  if (p.fast && a.block_size == 16 && (group == 2 || group == 4 || group == 8) &&
+      env_int("PKV_DECODE_TC", 1) != 0) {
+    // one CTA per (sequence, KV head, split of 8..32 pages)
+    p.tc = true;
+    int pps = 32;
+    while (pps > 8 && (int64_t)a.num_seqs * a.num_kv_heads * ((M + pps - 1) / pps) <
+                          env_int("PKV_DECODE_TARGET_CTAS", 888))
+      pps /= 2;
+    const int forced = env_int("PKV_DECODE_SPLIT_PAGES", 0);
+    if (forced > 0) pps = std::max(8, std::min(32, forced / 8 * 8));
+    p.pages_per_split = pps;
+    p.max_splits = std::max(1, (M + pps - 1) / pps);
+    return p;
   }
   p.max_splits = std::max(1, (M + p.pages_per_split - 1) / p.pages_per_split);
   if (p.fast && a.num_seqs <= kStreamMaxSeqs && env_int("PKV_DECODE_SPLIT", 0) == 0) {
@@ -1601,6 +1948,37 @@ int launch_fast_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_
       a.num_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq, a.sm_scale * kLog2e,
       p.pages_per_split, p.max_splits, device_error_word());
   return kOk;
+}
+
+template <int G>
+int launch_tc_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_ml,
+                cudaStream_t stream) {
+  using C = TcCfg<G>;
+  CUtensorMap mk, mv;
+  if (!cached_cache_map(&mk, a.k_cache, a.num_blocks, 16, a.num_kv_heads, 1) ||
+      !cached_cache_map(&mv, a.v_cache, a.num_blocks, 16, a.num_kv_heads, 1)) {
+    set_error("cuTensorMapEncodeTiled failed for the paged cache");
+    return kCudaError;
+  }
+  auto kern = decode_tc_kernel<G>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  dim3 grid(a.num_seqs, p.max_splits, a.num_kv_heads);
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(
+      mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out, ws_acc, ws_ml,
+      a.num_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq, a.sm_scale * kLog2e,
+      p.pages_per_split, p.max_splits, device_error_word());
+  return kOk;
+}
+
+int launch_tc(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_ml,
+              cudaStream_t stream) {
+  switch (a.num_heads / a.num_kv_heads) {
+    case 2: return launch_tc_t<2>(a, p, ws_acc, ws_ml, stream);
+    case 4: return launch_tc_t<4>(a, p, ws_acc, ws_ml, stream);
+    case 8: return launch_tc_t<8>(a, p, ws_acc, ws_ml, stream);
+  }
+  set_error("internal: no tensor-core decode instantiation for this group size");
+  return kUnsupported;
 }
 
 template <int BS, int HG>
@@ -1679,7 +2057,9 @@ int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
     ws_ml = reinterpret_cast<float2*>(base + slots * a.head_dim * sizeof(float));
   }
   int rc = kOk;
-  if (p.fast) {
+  if (p.tc) {
+    rc = launch_tc(a, p, ws_acc, ws_ml, stream);
+  } else if (p.fast) {
     rc = a.block_size == 16 ? dispatch_hg<16>(a, p, ws_acc, ws_ml, stream)
                             : dispatch_hg<32>(a, p, ws_acc, ws_ml, stream);
   } else {

@@ -225,16 +225,18 @@ __global__ void __launch_bounds__(kQThreads)
 // head_dim 128, 16-token blocks of at most kBulkMaxBlock bytes (fp16/bf16
 // with <= 9 KV heads, fp32 with <= 4): a persistent kernel streams whole
 // blocks (contiguous in the [NB, bs, Hkv, D] layout) into a ring of shared
-// memory stages with one cp.async.bulk each.  Two groups of eight warps take
-// alternate blocks; in a group a warp quantizes one head from shared memory
-// (absmax pass, then codes).  Deep queues with few registers: the register
-// kernel above keeps one block-head in flight per warp and its CTAs turn
-// over every few microseconds.
-constexpr int kBulkGroups = 2;
-constexpr int kBulkGroupWarps = 8;
-constexpr int kBulkConsumerWarps = kBulkGroups * kBulkGroupWarps;
+// memory stages with one cp.async.bulk each.  Sixteen consumer warps take
+// every block together, two per head (8 tokens each): absmax of the half,
+// exchange through shared memory, codes.  Every consumer warp passes every
+// stage phase in order -- a warp that skipped blocks could wait on a
+// stage's next phase while the current one is incomplete and, the parities
+// of phases k-1 and k+1 being equal, pass it early.  Deep queues with few
+// registers: the register kernel above keeps one block-head in flight per
+// warp and its CTAs turn over every few microseconds.
+constexpr int kBulkConsumerWarps = 16;
 constexpr int kBulkThreads = kBulkConsumerWarps * 32 + 32;
 constexpr uint32_t kBulkMaxBlock = 36 * 1024;
+constexpr int kBulkMaxHeads = 9;
 constexpr int kBulkStages = 3;
 
 template <typename T>
@@ -311,11 +313,12 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
   const uint32_t block_bytes = (uint32_t)(elems * sizeof(T));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kBulkStages * block_bytes);
   uint64_t* empty = full + kBulkStages;
+  uint32_t* s_half = reinterpret_cast<uint32_t*>(empty + kBulkStages);  // [2][heads][2]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < kBulkStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kBulkGroupWarps);
+      mbar_init(&empty[i], kBulkConsumerWarps);
     }
     mbar_fence_init();
   }
@@ -340,39 +343,46 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
     return;
   }
 
-  // block n of this CTA's sequence goes to group n % kBulkGroups
-  const int group = warp / kBulkGroupWarps;
-  const int gw = warp % kBulkGroupWarps;
+  const int h0 = warp % 8;      // heads h0, h0 + 8
+  const int half = warp / 8;    // tokens [8 * half, 8 * half + 8)
+  const int64_t tok = (int64_t)hkv * 128;
   bool live = true;
   int n = 0;
   for (int64_t b = blockIdx.x; b < nb; b += gridDim.x) {
     if (skip != nullptr && skip[b]) continue;
-    const bool mine = n % kBulkGroups == group;
     const int st = n % kBulkStages;
     const uint32_t ph = (uint32_t)(n / kBulkStages) & 1u;
+    uint32_t* amax_buf = s_half + (n & 1) * kBulkMaxHeads * 2;
     ++n;
-    if (!mine) continue;
     if (live && !mbar_wait_bounded(&full[st], ph, err)) {
       record_error(err, kDevWaitTimeout);
       live = false;
     }
+    const T* blk = reinterpret_cast<const T*>(smem_raw + st * block_bytes);
     if (live) {
-      const T* blk = reinterpret_cast<const T*>(smem_raw + st * block_bytes);
-      for (int h = gw; h < hkv; h += kBulkGroupWarps) {
-        const T* row0 = blk + (int64_t)h * 128 + lane * 4;
-        const int64_t tok = (int64_t)hkv * 128;
+      for (int h = h0; h < hkv; h += 8) {
+        const T* row0 = blk + (int64_t)(8 * half) * tok + (int64_t)h * 128 + lane * 4;
         uint32_t m = absmax_bits4<T>(row0);
-#pragma unroll 5
-        for (int t = 1; t < BS; ++t) m = absmax_fold<T>(m, absmax_bits4<T>(row0 + t * tok));
+#pragma unroll
+        for (int t = 1; t < 8; ++t) m = absmax_fold<T>(m, absmax_bits4<T>(row0 + t * tok));
         m = __reduce_max_sync(0xffffffffu, absmax_float_bits<T>(m));  // NaN wins
-        const float amax = __uint_as_float(m);
+        if (lane == 0) amax_buf[h * 2 + half] = m;
+      }
+    }
+    // both halves of every head published (amax_buf alternates per block, so
+    // this one barrier also keeps the next block from overwriting it early)
+    named_barrier(1, kBulkConsumerWarps * 32);
+    if (live) {
+      for (int h = h0; h < hkv; h += 8) {
+        const float amax = __uint_as_float(max(amax_buf[h * 2], amax_buf[h * 2 + 1]));
         const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-        if (lane == 0) scale[b * hkv + h] = s;
+        if (lane == 0 && half == 0) scale[b * hkv + h] = s;
         const float rcp = __frcp_rn(s);
         const bool fast = isfinite(amax) && !isinf(rcp);
-        int8_t* out = q + b * elems + (int64_t)h * 128 + lane * 4;
+        const T* row0 = blk + (int64_t)(8 * half) * tok + (int64_t)h * 128 + lane * 4;
+        int8_t* out = q + b * elems + (int64_t)(8 * half) * tok + (int64_t)h * 128 + lane * 4;
 #pragma unroll 2
-        for (int t = 0; t < BS; ++t) {
+        for (int t = 0; t < 8; ++t) {
           float f[4];
           load4_shared<T>(row0 + t * tok, f);
           *reinterpret_cast<uint32_t*>(out + t * tok) = quantize_word(f, s, rcp, fast);
@@ -397,10 +407,11 @@ int launch_quantize_t(const T* kv, int8_t* q, float* scale, int64_t nb, int bs, 
                       const uint8_t* skip, cudaStream_t stream) {
   constexpr int VEC = 16 / sizeof(T);
   const uint64_t block_bytes = (uint64_t)bs * hkv * hd * sizeof(T);
-  if (hd == 128 && bs == 16 && block_bytes <= kBulkMaxBlock &&
+  if (hd == 128 && bs == 16 && block_bytes <= kBulkMaxBlock && hkv <= kBulkMaxHeads &&
       reinterpret_cast<uintptr_t>(kv) % 16 == 0 && reinterpret_cast<uintptr_t>(q) % 4 == 0 &&
       std::getenv("PKV_QUANTIZE_REGISTER") == nullptr) {
-    const size_t smem = kBulkStages * block_bytes + 2 * kBulkStages * sizeof(uint64_t);
+    const size_t smem = kBulkStages * block_bytes + 2 * kBulkStages * sizeof(uint64_t) +
+                        2 * kBulkMaxHeads * 2 * sizeof(uint32_t);
     auto kern = quantize_bulk_kernel<T>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t ctas = std::min<int64_t>(nb, 2LL * sm_count_quant());

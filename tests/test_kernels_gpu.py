@@ -342,6 +342,35 @@ def test_attention_stream_one_sequence_over_all_ctas(cuda):
         assert torch.equal(o, outs[0])
 
 
+@pytest.mark.parametrize("group", [2, 4, 8])
+@pytest.mark.parametrize("pages", ["auto", "8", "16", "32"])
+def test_attention_tensor_core_gqa(cuda, monkeypatch, group, pages):
+    """GQA groups of 2/4/8 query heads per KV head run on the tcgen05 kernel
+    (q.K and p.V as int8 MMAs into tensor memory); ragged lengths, partial
+    128-token tiles, one to four tiles per split, several splits."""
+    if pages != "auto":
+        monkeypatch.setenv("PKV_DECODE_SPLIT_PAGES", pages)
+    from pagedkv_fusion import _C
+    for seed, S, hkv, L in ((31, 7, 4, 1500), (32, 3, 2, 130), (33, 12, 8, 700), (34, 2, 1, 17)):
+        assert _C.quant_paged_attention_kernel_launches(S, group * hkv, hkv, 128, 16, 94) == 2
+        prob = problems.make_paged_kv_problem(np.random.default_rng(seed), S, group * hkv, hkv,
+                                              128, 16, L)
+        args = quantized_problem(*prob)
+        assert_attention_close(run_attention(args), c_oracle.paged_attention(*args))
+
+
+def test_attention_tensor_core_matches_cuda_core_path(cuda, monkeypatch):
+    """The tensor-core and CUDA-core kernels use the same integer formats:
+    their outputs agree to fp32 rounding."""
+    prob = problems.make_paged_kv_problem(np.random.default_rng(35), 9, 32, 8, 128, 16, 2100)
+    args = quantized_problem(*prob)
+    tc = run_attention(args)
+    monkeypatch.setenv("PKV_DECODE_TC", "0")
+    cc = run_attention(args)
+    scale = float(cc.abs().max())
+    assert float((tc - cc).abs().max()) / scale < 2e-6
+
+
 @pytest.mark.parametrize("pages", ["1", "2", "8", "32"])
 def test_attention_split_sizes(cuda, monkeypatch, pages):
     monkeypatch.setenv("PKV_DECODE_SPLIT", "1")
