@@ -361,6 +361,26 @@ def eviction_bench(torch, C, ops, iters: int = 200):
         ops.select_eviction_candidates(s, k)
         torch.cuda.synchronize()
         wall.append((time.perf_counter() - t0) * 1e6)
+    # attention statistics derived from an fp16 K pool of the same shape
+    # (16,384 blocks x 16 tokens x 8 KV heads x 128): the HBM-bound producer
+    # of the attention term
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    kpool = torch.randn((16384, 16, 8, 128), generator=g, device="cuda").half()
+    qh = torch.randn((8, 128), generator=g, device="cuda")
+    for _ in range(5):
+        C.attention_stats(kpool, qh, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    st_us = []
+    for _ in range(50):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        C.attention_stats(kpool, qh, 1 / math.sqrt(128))
+        e1.record()
+        e1.synchronize()
+        st_us.append(e0.elapsed_time(e1) * 1e3)
+    stats_bytes = kpool.numel() * 2 + 16384 * 16 * 8 * 4 * 2 + 16384 * 16 * 4
+    del kpool
     cpu = []
     for _ in range(50):
         t0 = time.perf_counter()
@@ -373,7 +393,11 @@ def eviction_bench(torch, C, ops, iters: int = 200):
             "graph_wall_p50_us": statistics.median(graph_wall),
             "wall_p50_us": statistics.median(wall),
             "wall_p90_us": statistics.quantiles(wall, n=10)[8],
-            "cpu_port_p50_us": statistics.median(cpu)}
+            "cpu_port_p50_us": statistics.median(cpu),
+            "attention_stats_from_fp16_k": {
+                "device_p50_us": statistics.median(st_us),
+                "gb_s": stats_bytes / (statistics.median(st_us) / 1e6) / 1e9,
+                "bytes": stats_bytes}}
 
 
 def run_gpu_arm(args):

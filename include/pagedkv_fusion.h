@@ -138,6 +138,27 @@ int pkv_quantize_kv_per_block(const void *kv, int32_t kv_dtype, int8_t *q,
                               int32_t head_dim, void *stream);
 
 /*
+ * Per-token attention statistics derived from the keys, the input the
+ * eviction score's attention term reads: for a K pool [num_blocks,
+ * block_size, num_kv_heads, 128] (float32 / float16 / bfloat16, dtype codes
+ * as for quantization) and one query vector per KV head q [num_kv_heads,
+ * 128] float32,
+ *   s_h[b, t]  = sm_scale * (q_h . K[b, t, h, :])
+ *   attn[b, t] = mean_h exp(s_h[b, t] - max over the pool of s_h)
+ * written to attn [num_blocks, block_size] float32, in (0, 1].  block_size
+ * 16 or 32.  The workspace holds the logits and the per-head maxima.  No
+ * counterpart in the reference, whose eviction statistics are given arrays
+ * (pagedkv_fusion/reference.py:38-71); the definition is this library's.
+ */
+size_t pkv_attention_stats_workspace_size(int64_t num_blocks,
+                                          int32_t block_size,
+                                          int32_t num_kv_heads);
+int pkv_attention_stats(const void *k, int32_t k_dtype, const float *q,
+                        float *attn, int64_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, float sm_scale,
+                        void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * pkv_quantize_kv_per_block for the blocks whose skip[b] byte is zero;
  * blocks with a nonzero byte are neither read nor written (their codes and
  * scale keep whatever they held).  Quantizes the blocks that survive an

@@ -49,6 +49,7 @@ __all__ = [
     "mark_blocks",
     "compact_block_tables",
     "evict_quantize_decode",
+    "attention_stats",
 ]
 
 
@@ -325,3 +326,21 @@ def evict_quantize_decode(q, k, v, recency, frequency, attn_weights, valid_mask,
     tables, lens = compact_block_tables(block_tables, seq_lens, mask, k.shape[1])
     out = paged_attention(q, kq, ks, vq, vs, tables, lens, sm_scale)
     return out, ids, tables, lens
+
+
+# ---------------------------------------------------------------------------
+# Attention statistics derived from the keys (no reference counterpart: the
+# reference's eviction statistics are given arrays, reference.py:38-71).
+# Definition of this library, restated here in float64.
+# ---------------------------------------------------------------------------
+
+def attention_stats(k, q, sm_scale):
+    """attn[b, t] = mean_h exp(s_h[b, t] - max s_h), s_h = sm_scale * q_h . K[b, t, h].
+
+    ``k`` [nb, bs, Hkv, D] (any float dtype), ``q`` [Hkv, D]; float32 [nb, bs].
+    """
+    kk = np.asarray(k, dtype=np.float64)
+    qq = np.asarray(q, dtype=np.float64)
+    s = np.einsum("bthd,hd->bth", kk, qq) * float(sm_scale)
+    m = s.reshape(-1, s.shape[2]).max(axis=0)
+    return np.exp(s - m[None, None, :]).mean(axis=2).astype(np.float32)

@@ -208,6 +208,33 @@ int pkv_quantize_kv_per_block_except(const void* kv, int32_t kv_dtype, const uin
                           skip, stream);
 }
 
+size_t pkv_attention_stats_workspace_size(int64_t num_blocks, int32_t block_size,
+                                          int32_t num_kv_heads) {
+  if (num_blocks <= 0 || block_size <= 0 || num_kv_heads <= 0) return 0;
+  return pkv::attention_stats_workspace_size(num_blocks, block_size, num_kv_heads);
+}
+
+int pkv_attention_stats(const void* k, int32_t k_dtype, const float* q, float* attn,
+                        int64_t num_blocks, int32_t block_size, int32_t num_kv_heads,
+                        int32_t head_dim, float sm_scale, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  clear_error();
+  if (num_blocks < 0 || num_kv_heads <= 0)
+    return fail(PKV_ERR_INVALID_ARGUMENT, "expected K [nb, bs, nkv, 128] and q [nkv, 128]");
+  if (head_dim != 128) return fail(PKV_ERR_UNSUPPORTED, "attention statistics need head_dim 128");
+  if (block_size != 16 && block_size != 32)
+    return fail(PKV_ERR_UNSUPPORTED, "attention statistics need block_size 16 or 32");
+  if (k_dtype < 0 || k_dtype > 2)
+    return fail(PKV_ERR_INVALID_ARGUMENT, "k must be float32, float16 or bfloat16");
+  if (num_blocks > 0 && (!k || !q || !attn))
+    return fail(PKV_ERR_INVALID_ARGUMENT, "null input or output pointer");
+  const size_t elem = k_dtype == 0 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(k) % (4 * elem) != 0 || reinterpret_cast<uintptr_t>(q) % 16 != 0)
+    return fail(PKV_ERR_INVALID_ARGUMENT, "k and q must be aligned to 4 elements / 16 bytes");
+  return pkv::launch_attention_stats(k, k_dtype, q, attn, num_blocks, block_size, num_kv_heads,
+                                     sm_scale, workspace, workspace_bytes, as_stream(stream));
+}
+
 int pkv_mark_blocks(const int64_t* ids, int64_t num_ids, int64_t id_offset, int64_t num_blocks,
                     uint8_t* mask, void* stream) {
   clear_error();

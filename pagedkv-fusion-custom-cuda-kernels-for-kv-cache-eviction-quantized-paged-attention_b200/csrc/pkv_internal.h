@@ -24,6 +24,12 @@ int launch_quantize(const void* kv, int dtype, int8_t* q, float* scale, int64_t 
                     int block_size, int num_kv_heads, int head_dim, const uint8_t* skip,
                     cudaStream_t stream);
 
+// ---- attn_stats.cu ------------------------------------------------------------
+size_t attention_stats_workspace_size(int64_t num_blocks, int block_size, int num_kv_heads);
+int launch_attention_stats(const void* k, int dtype, const float* q, float* attn,
+                           int64_t num_blocks, int block_size, int num_kv_heads, float sm_scale,
+                           void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 // ---- compose.cu -------------------------------------------------------------
 int launch_mark_blocks(const int64_t* ids, int64_t n, int64_t id_offset, int64_t num_blocks,
                        uint8_t* mask, cudaStream_t stream);

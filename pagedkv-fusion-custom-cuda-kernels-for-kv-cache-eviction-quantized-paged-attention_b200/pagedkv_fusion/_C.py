@@ -53,6 +53,8 @@ _attn_launches = _sig("pkv_quant_paged_attention_kernel_launches", [_I32] * 6, c
 _quant_except = _sig("pkv_quantize_kv_per_block_except",
                      [_P, _I32, _P, _P, _P, _I64, _I32, _I32, _I32, _P])
 _mark = _sig("pkv_mark_blocks", [_P, _I64, _I64, _I64, _P, _P])
+_stats_ws = _sig("pkv_attention_stats_workspace_size", [_I64, _I32, _I32], _SZ)
+_stats = _sig("pkv_attention_stats", [_P, _I32, _P, _P, _I64, _I32, _I32, _I32, _F, _P, _SZ, _P])
 _compact = _sig("pkv_compact_block_tables", [_P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _P])
 _attn = _sig("pkv_quant_paged_attention",
              [_P] * 8 + [_I32] * 5 + [_I64, _I32, _F, _P, _SZ, _P])
@@ -240,6 +242,22 @@ def quantize_kv_per_block_except(kv, skip, out_q, out_scale):
     _check(_quant_except(x.data_ptr(), _DTYPE_CODE[x.dtype], skip.data_ptr(), out_q.data_ptr(),
                          out_scale.data_ptr(), nb, bs, nkv, hd, _stream(x)))
     return out_q, out_scale
+
+
+def attention_stats(k, q, sm_scale: float):
+    """Per-token attention weights ``[num_blocks, block_size]`` derived from the
+    key pool ``k`` ``[nb, bs, Hkv, 128]`` and one query per KV head ``q``
+    ``[Hkv, 128]``: mean over heads of exp(s - max s), s = sm_scale * q.k."""
+    _require(k.is_cuda and q.is_cuda, "k and q must be CUDA tensors")
+    _require(k.dim() == 4 and k.dtype in _DTYPE_CODE, "k must be [nb, bs, nkv, hd] float32/16/bf16")
+    nb, bs, nkv, hd = k.shape
+    _require(q.dtype == torch.float32 and tuple(q.shape) == (nkv, hd), "q must be float32 [nkv, hd]")
+    kc, qc = k.contiguous(), q.contiguous()
+    attn = torch.empty((nb, bs), dtype=torch.float32, device=kc.device)
+    ws, wp = _workspace(_stats_ws(nb, bs, nkv), kc.device)
+    _check(_stats(kc.data_ptr(), _DTYPE_CODE[kc.dtype], qc.data_ptr(), attn.data_ptr(), nb, bs,
+                  nkv, hd, float(sm_scale), wp, 0 if ws is None else ws.numel(), _stream(kc)))
+    return attn
 
 
 def mark_blocks(ids, id_offset: int, num_blocks: int):

@@ -36,6 +36,7 @@ __all__ = [
     "select_eviction_candidates",
     "eviction_scores_and_candidates",
     "EvictionPlan",
+    "attention_stats",
     "quant_paged_attention",
 ]
 
@@ -152,6 +153,19 @@ def eviction_scores_and_candidates(recency, frequency, attn_weights, valid_mask,
                                            st.to_device(valid_mask, torch.bool), int(k),
                                            w_recency, w_frequency, w_attention)
     return st.back(scores), st.back(idx)
+
+
+def attention_stats(k, q, sm_scale: float):
+    """Per-token attention weights of a key pool for the eviction score
+    (``attn_weights``): mean over KV heads of exp(s - max s) with
+    s = sm_scale * q_h . K[b, t, h].  ``k`` ``[nb, bs, Hkv, 128]``, ``q``
+    ``[Hkv, 128]``; returns float32 ``[nb, bs]`` in (0, 1]."""
+    C = _lib()
+    if _all_cuda(k, q):
+        return C.attention_stats(k, q, sm_scale)
+    st = _Staging(k, q)
+    kd = k if isinstance(k, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(k))
+    return st.back(C.attention_stats(kd.to(st.device), st.to_device(q, torch.float32), sm_scale))
 
 
 class EvictionPlan:

@@ -90,3 +90,32 @@ def test_composition_evicts_the_lowest_scores():
     assert np.array_equal(ids, O.select_eviction_candidates(scores, n_ev))
     assert not np.isin(tables[tables >= 0], ids).any()
     assert out.shape == q.shape and np.isfinite(out).all()
+
+
+def test_report_memory_section_matches_reference_arithmetic():
+    """The report's memory rows (pure arithmetic) carry the reference
+    driver's keys and values (benchmarks/bench_quant_attention.py:36-56)."""
+    from pagedkv_fusion import report
+    rows = report.measure_memory([dict(num_blocks=4096, block_size=16, num_kv_heads=8,
+                                       head_dim=128)])
+    r = rows[0]
+    assert set(r) >= {"fp16_MiB", "int8_MiB", "savings_pct", "num_blocks"}
+    assert r["fp16_MiB"] == 2 * 4096 * 16 * 8 * 128 * 2 / 2**20
+    assert r["int8_MiB"] == (2 * 4096 * 16 * 8 * 128 + 2 * 4096 * 8 * 4) / 2**20
+    assert abs(r["savings_pct"] - 100 * (1 - r["int8_MiB"] / r["fp16_MiB"])) < 1e-12
+
+
+def test_attention_stats_definition_properties():
+    rng = np.random.default_rng(9)
+    k = rng.standard_normal((40, 16, 4, 128)).astype(np.float16)
+    q = rng.standard_normal((4, 128)).astype(np.float32)
+    a = O.attention_stats(k, q, 1 / np.sqrt(128))
+    assert a.shape == (40, 16) and a.dtype == np.float32
+    assert (a > 0).all() and (a <= 1).all()
+    # each head's most-attended token contributes exp(0) = 1 to its mean
+    s = np.einsum("bthd,hd->bth", k.astype(np.float64), q.astype(np.float64))
+    for h in range(4):
+        b, t = np.unravel_index(np.argmax(s[:, :, h]), s.shape[:2])
+        assert a[b, t] >= 1 / 4 - 1e-7
+    # a larger query sharpens the distribution: the mean weight drops
+    assert O.attention_stats(k, q * 4, 1 / np.sqrt(128)).mean() < a.mean()

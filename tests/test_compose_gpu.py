@@ -175,3 +175,42 @@ def test_quantize_rounding_window_and_special_values(cuda, monkeypatch, register
             if fin[b, h]:
                 assert np.array_equal(gq[b, :, h], want_q[b, :, h]), (b, h)
     assert np.array_equal(got_s.cpu().numpy().view(np.uint32), want_s.view(np.uint32))
+
+
+def test_report_sections(cuda, tmp_path):
+    """The memory / quality / speed report runs on the native kernels and
+    emits the reference driver's keys; INT8 error against fp32 attention is
+    what per-block INT8 K/V costs (well under the output spread)."""
+    from pagedkv_fusion import report
+    out = tmp_path / "r.json"
+    assert report.main(["--out", str(out), "--speed-iters", "2"]) == 0
+    import json
+    rep = json.loads(out.read_text())
+    assert set(rep) == {"memory", "quality", "speed"}
+    for row in rep["quality"]:
+        assert set(row) == {"distribution", "rmse", "max_abs", "out_std"}
+        assert row["rmse"] < 0.05 * row["out_std"]
+    for row in rep["speed"]:
+        assert {"num_seqs", "seq_len", "int8_kernel_p50_ms", "fp16_sdpa_gathered_p50_ms"} <= set(row)
+
+
+@pytest.mark.parametrize("dtype,bs,heads", [(torch.float16, 16, 8), (torch.float32, 16, 3),
+                                            (torch.bfloat16, 32, 8), (torch.float16, 32, 40)])
+def test_attention_stats_match_oracle(cuda, dtype, bs, heads):
+    """Key-derived attention statistics (the eviction score's attention
+    input) against the float64 restatement; then fed to the fused scorer."""
+    rng = np.random.default_rng(heads + bs)
+    nb = 777
+    k = torch.from_numpy(rng.standard_normal((nb, bs, heads, 128), dtype=np.float32)).to(dtype)
+    q = rng.standard_normal((heads, 128)).astype(np.float32)
+    got = cuda.attention_stats(k.cuda(), dev(q), 1 / np.sqrt(128)).cpu().numpy()
+    want = O.attention_stats(k.float().numpy(), q, 1 / np.sqrt(128))
+    np.testing.assert_allclose(got, want, rtol=2e-5, atol=1e-7)
+    assert (got > 0).all() and (got <= 1).all()
+    # the statistics are a valid input to the bit-exact eviction scorer
+    rec = rng.random(nb, dtype=np.float32)
+    freq = rng.random(nb, dtype=np.float32)
+    valid = np.ones((nb, bs), bool)
+    scores = cuda.eviction_scores(dev(rec), dev(freq), dev(got), dev(valid)).cpu().numpy()
+    assert np.array_equal(scores.view(np.uint32),
+                          O.eviction_scores(rec, freq, got, valid).view(np.uint32))
