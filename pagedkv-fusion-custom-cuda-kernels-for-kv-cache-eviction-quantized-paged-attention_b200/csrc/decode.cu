@@ -1490,15 +1490,21 @@ __global__ void __launch_bounds__(128)
 // quarter) turn logits into probabilities and read the results; partials
 // go through decode_combine_kernel.
 
-template <int G>
+// STAGES page-tile stages per CTA; MINB CTAs per SM (launch bound); splits
+// of at most MAXTILES 128-token tiles.  Several small CTAs per SM (2 stages
+// each: the bytes in flight per SM of 2 CTAs with 4) overlap each other's
+// prologue, softmax and epilogue.  Groups of 8 take 2-tile splits, so that
+// 3 CTAs fit the SM's registers and tensor memory.
+template <int G, int STAGES = 2, int MINB = (G <= 4 ? 4 : 3), int MAXTILES = (G <= 4 ? 4 : 2)>
 struct TcCfg {
   static constexpr int kNQ = G * 3 <= 8 ? 8 : (G * 3 <= 16 ? 16 : 32);  // MMA N
   static constexpr int kTileTok = 128;
   static constexpr int kPagesPerTile = 8;
-  static constexpr int kMaxTiles = 4;
+  static constexpr int kMaxTiles = MAXTILES;
   static constexpr int kMaxTok = kMaxTiles * kTileTok;
   static constexpr int kMaxPages = kMaxTiles * kPagesPerTile;
-  static constexpr int kStages = 4;
+  static constexpr int kStages = STAGES;
+  static constexpr int kMinBlocks = MINB;
   static constexpr int kThreads = 256;
   static constexpr int kRowBytes = ((kNQ * 128 + 1023) / 1024) * 1024;  // one operand tile
   static constexpr int kOffQ = kStages * kStageBytes;
@@ -1516,13 +1522,47 @@ struct TcCfg {
   // D1: one kNQ-column slice per K tile, then D2
   static constexpr int kD2Col = kMaxTiles * kNQ;
   static constexpr int kTmemCols = (kD2Col + kNQ) <= 64 ? 64 : ((kD2Col + kNQ) <= 128 ? 128 : 256);
-  static_assert(2 * (kSmemBytes + 1024) <= 228 * 1024, "two CTAs per SM");
-  static_assert(3 * kTmemCols <= 512 || 3 * (kSmemBytes + 1024) > 228 * 1024,
-                "CTAs that fit on an SM must fit in its tensor memory");
+  static_assert(kMinBlocks * (kSmemBytes + 1024) <= 228 * 1024, "CTAs per SM by shared memory");
+  static_assert((kMinBlocks + 1) * kTmemCols <= 512 ||
+                    (kMinBlocks + 1) * (kSmemBytes + 1024) > 228 * 1024,
+                "every CTA that fits on an SM must fit in its tensor memory");
+  static_assert(kMinBlocks * kTmemCols <= 512, "tensor memory for kMinBlocks CTAs");
 };
 
+// Calls f(g, v) for each query head g of a TMEM accumulator row holding the
+// three digit / plane columns 3g, 3g + 1, 3g + 2 (v = c2 * 65536 + c1 * 256
+// + c0 as float).  Rows wider than 16 columns are read in two 16-aligned
+// loads; the group straddling them (columns 15-17) is assembled from both.
+template <int G, int NQ, typename F>
+__device__ __forceinline__ void tmem_row_groups(uint32_t taddr, F f) {
+  auto combine = [](uint32_t c0, uint32_t c1, uint32_t c2) {
+    return (float)(int)c2 * 65536.0f + ((float)(int)c1 * 256.0f + (float)(int)c0);
+  };
+  if constexpr (NQ <= 16) {
+    uint32_t r[NQ];
+    tmem_load<NQ>(taddr, r);
+    tmem_wait_load();
+#pragma unroll
+    for (int g = 0; g < G; ++g) f(g, combine(r[3 * g], r[3 * g + 1], r[3 * g + 2]));
+  } else {
+    static_assert(NQ == 32 && G >= 6 && G <= 10, "two-slice rows");
+    uint32_t a[16];
+    tmem_load<16>(taddr, a);
+    tmem_wait_load();
+#pragma unroll
+    for (int g = 0; g < 5; ++g) f(g, combine(a[3 * g], a[3 * g + 1], a[3 * g + 2]));
+    const uint32_t c15 = a[15];
+    uint32_t b[16];
+    tmem_load<16>(taddr + 16, b);
+    tmem_wait_load();
+    f(5, combine(c15, b[0], b[1]));
+#pragma unroll
+    for (int g = 6; g < G; ++g) f(g, combine(b[3 * g - 16], b[3 * g - 15], b[3 * g - 14]));
+  }
+}
+
 template <int G>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(256, TcCfg<G>::kMinBlocks)
     decode_tc_kernel(const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q,
                      const float* __restrict__ k_scale, const float* __restrict__ v_scale,
@@ -1707,21 +1747,15 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
     for (int g = 0; g < G; ++g) kmax[g] = -INFINITY;
     for (int ti = 0; ti < n_tiles; ++ti) {
-      uint32_t r[NQ];
-      tmem_load<NQ>(tmem + lane_base + ti * NQ, r);
-      tmem_wait_load();
       const int tok = ti * C::kTileTok + e;
       const int pg = min(tok / BS, C::kMaxPages - 1);
       const bool valid = live && tok < T && s_phys[pg] >= 0;
       const float ks = s_ks[pg];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float v = (float)(int)r[3 * g + 2] * 65536.0f +
-                        ((float)(int)r[3 * g + 1] * 256.0f + (float)(int)r[3 * g]);
+      tmem_row_groups<G, NQ>(tmem + lane_base + ti * NQ, [&](int g, float v) {
         const float logit = valid ? v * (s_qs[g] * ks * qk_scale) : -INFINITY;
         s_logit[g * C::kMaxTok + tok] = logit;
         kmax[g] = fmaxf(kmax[g], logit);
-      }
+      });
     }
     float* red_m = s_red;
     float* red_l = s_red + 32;
@@ -1774,14 +1808,9 @@ __global__ void __launch_bounds__(256, 2)
       live = false;
     }
     tmem_fence_after_sync();
-    uint32_t r[NQ];
-    tmem_load<NQ>(tmem + lane_base + C::kD2Col, r);
-    tmem_wait_load();
     const float back = vmax * (1.0f / 16777215.0f);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float acc = ((float)(int)r[3 * g + 2] * 65536.0f +
-                         ((float)(int)r[3 * g + 1] * 256.0f + (float)(int)r[3 * g])) * back;
+    tmem_row_groups<G, NQ>(tmem + lane_base + C::kD2Col, [&](int g, float v) {
+      const float acc = v * back;
       const int hq = j * G + g;
       if (n_splits == 1) {
         out[((int64_t)seq * num_heads + hq) * 128 + e] = l[g] > 0.0f ? acc / l[g] : 0.0f;
@@ -1790,7 +1819,7 @@ __global__ void __launch_bounds__(256, 2)
         ws_acc[slot * 128 + e] = acc;
         if (e == 0) ws_ml[slot] = make_float2(m[g], l[g]);
       }
-    }
+    });
   }
   tmem_fence_before_sync();
   __syncthreads();
@@ -1873,12 +1902,14 @@ Plan make_plan(const DecodeArgs& a) {
       env_int("PKV_DECODE_TC", 1) != 0) {
     // one CTA per (sequence, KV head, split of 8..32 pages)
     p.tc = true;
-    int pps = 32;
+    int pps = group <= 4 ? TcCfg<4>::kMaxPages : TcCfg<8>::kMaxPages;
     while (pps > 8 && (int64_t)a.num_seqs * a.num_kv_heads * ((M + pps - 1) / pps) <
                           env_int("PKV_DECODE_TARGET_CTAS", 888))
       pps /= 2;
     const int forced = env_int("PKV_DECODE_SPLIT_PAGES", 0);
-    if (forced > 0) pps = std::max(8, std::min(32, forced / 8 * 8));
+    if (forced > 0)
+      pps = std::max(8, std::min(group <= 4 ? TcCfg<4>::kMaxPages : TcCfg<8>::kMaxPages,
+                                 forced / 8 * 8));
     p.pages_per_split = pps;
     p.max_splits = std::max(1, (M + pps - 1) / pps);
     return p;
