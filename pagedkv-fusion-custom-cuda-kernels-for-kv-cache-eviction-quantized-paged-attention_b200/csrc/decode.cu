@@ -1615,15 +1615,25 @@ __global__ void __launch_bounds__(256, TcCfg<G>::kMinBlocks)
     mbar_fence_init();
   }
   if (warp == 1) tmem_alloc(s_tmem, C::kTmemCols);
-  if (warp == 2 || warp == 3) {  // the split's block ids and scales
-    for (int pg = tid - 64; pg < np; pg += 64) {
+  if (warp == 0) {  // the split's block ids: all the page loads need
+    for (int pg = lane; pg < np; pg += 32) {
       const int phys = block_tables[(int64_t)seq * max_blocks_per_seq + p0 + pg];
       const bool ok = phys >= 0 && (int64_t)phys < num_blocks;
       if (!ok) record_error(err, kDevBadBlockId);
       s_phys[pg] = ok ? phys : -1;
-      const int64_t si = (int64_t)(ok ? phys : 0) * num_kv_heads + j;
-      s_ks[pg] = ok ? k_scale[si] : 0.0f;
-      s_vs[pg] = ok ? v_scale[si] : 0.0f;
+    }
+  }
+  tmem_fence_before_sync();
+  __syncthreads();  // barriers initialized, block ids and TMEM base published
+  tmem_fence_after_sync();
+  // The page loads start now; scales and query digits load meanwhile and are
+  // published to the MMA and epilogue warps (1-7) by named barrier 2.
+  if (warp == 2 || warp == 3) {
+    for (int pg = tid - 64; pg < np; pg += 64) {
+      const int phys = s_phys[pg];
+      const int64_t si = (int64_t)(phys >= 0 ? phys : 0) * num_kv_heads + j;
+      s_ks[pg] = phys >= 0 ? k_scale[si] : 0.0f;
+      s_vs[pg] = phys >= 0 ? v_scale[si] : 0.0f;
     }
   }
   if (warp >= 4) {  // query digit planes: row 3g + plane of the B operand
@@ -1650,11 +1660,9 @@ __global__ void __launch_bounds__(256, TcCfg<G>::kMinBlocks)
     }
     for (int r = 3 * G + w4; r < NQ; r += 4)  // padding rows
       *reinterpret_cast<uint32_t*>(s_q + sw128_offset(r, 4 * lane)) = 0u;
+    fence_proxy_async_smem();  // the digit planes are an MMA operand
   }
-  fence_proxy_async_smem();
-  tmem_fence_before_sync();
-  __syncthreads();
-  tmem_fence_after_sync();
+  if (warp >= 1) named_barrier(2, C::kThreads - 32);
   const uint32_t tmem = *s_tmem;
 
   if (warp == 0) {
@@ -1826,6 +1834,441 @@ __global__ void __launch_bounds__(256, TcCfg<G>::kMinBlocks)
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// Persistent form: CTAs walk their share of the (sequence, KV head, split)
+// units, so the page ring stays busy from one unit to the next.
+// ---------------------------------------------------------------------------
+//
+// Unit k of a CTA is its k-th non-empty unit of c, c + C, c + 2C, ...  Two
+// table warps fill the unit's half of a double-buffered table (block ids,
+// scales, token count and the query digit planes) and publish it on
+// meta_full[k & 1]; the half is released on meta_free[k & 1] by the TMA
+// warp (its loads issued), the MMA lane (a commit: its q.K MMAs completed)
+// and the epilogue (softmax done).  Per unit the MMA lane runs q.K into D1
+// (after the epilogue has read the previous unit's D1: d1_free), then p.V
+// into D2 (after p_ready); the epilogue reads D1 (k_done), writes the
+// probability planes, reads D2 (pv_done).  Each of those barriers completes
+// once per unit and its waiters are at most one phase behind, so parity
+// waits cannot alias.  Asynchronous (commit) arrivals target only stages
+// and table halves that a later tile or unit of the same CTA reuses.
+
+template <int G>
+struct TcsCfg {
+  static constexpr int kNQ = G * 3 <= 8 ? 8 : (G * 3 <= 16 ? 16 : 32);
+  static constexpr int kTileTok = 128;
+  static constexpr int kPagesPerTile = 8;
+  static constexpr int kMaxTiles = G <= 4 ? 4 : 2;
+  static constexpr int kMaxTok = kMaxTiles * kTileTok;
+  static constexpr int kMaxPages = kMaxTiles * kPagesPerTile;
+  static constexpr int kStages = 3;
+  static constexpr int kMinBlocks = 3;
+  static constexpr int kThreads = 256;
+  static constexpr int kRowBytes = ((kNQ * 128 + 1023) / 1024) * 1024;
+  // table halves: the query digit tiles (1 KB aligned, an MMA operand), and
+  // apart from them block ids, scales, per-head q scale, token count and
+  // largest V scale
+  static constexpr int kOffQ = kStages * kStageBytes;
+  static constexpr int kMetaPhys = 0;
+  static constexpr int kMetaKs = kMetaPhys + kMaxPages * 4;
+  static constexpr int kMetaVs = kMetaKs + kMaxPages * 4;
+  static constexpr int kMetaQs = kMetaVs + kMaxPages * 4;
+  static constexpr int kMetaT = kMetaQs + 32;
+  static constexpr int kMetaBytes = (kMetaT + 16 + 15) & ~15;
+  static constexpr int kOffMeta = kOffQ + 2 * kRowBytes;
+  static constexpr int kOffP = ((kOffMeta + 2 * kMetaBytes + 1023) / 1024) * 1024;
+  static constexpr int kOffLogit = kOffP + kMaxTiles * kRowBytes;
+  static constexpr int kOffRed = kOffLogit + G * kMaxTok * 4;
+  static constexpr int kOffTmem = kOffRed + 2 * 4 * 8 * 4;
+  static constexpr int kOffBar = kOffTmem + 16;
+  // full[S], empty[S], meta_full[2], meta_free[2], k_done, d1_free, p_ready, pv_done
+  static constexpr int kNumBars = 2 * kStages + 8;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 1024;
+  static constexpr int kD2Col = kMaxTiles * kNQ;
+  static constexpr int kTmemCols = (kD2Col + kNQ) <= 64 ? 64 : ((kD2Col + kNQ) <= 128 ? 128 : 256);
+  static_assert(kMinBlocks * (kSmemBytes + 1024) <= 228 * 1024, "CTAs per SM by shared memory");
+  static_assert((kMinBlocks + 1) * kTmemCols <= 512 ||
+                    (kMinBlocks + 1) * (kSmemBytes + 1024) > 228 * 1024,
+                "every CTA that fits on an SM must fit in its tensor memory");
+  static_assert(kMinBlocks * kTmemCols <= 512, "tensor memory");
+};
+
+// Unit u -> (sequence, KV head, split) and its page range; false if empty.
+struct TcsUnit {
+  int seq, j, split, p0, np, T, n_splits, n_tiles;
+};
+__device__ __forceinline__ bool tcs_unit(int64_t u, int hkv, int max_splits, int pps,
+                                         const int32_t* seq_lens, int max_blocks_per_seq,
+                                         TcsUnit& r) {
+  const int64_t per_seq = (int64_t)hkv * max_splits;
+  r.seq = (int)(u / per_seq);
+  const int rem = (int)(u - (int64_t)r.seq * per_seq);
+  r.j = rem / max_splits;
+  r.split = rem % max_splits;
+  const int L = max(seq_lens[r.seq], 0);
+  const int n_pages = covered_pages(L, 16, max_blocks_per_seq);
+  r.n_splits = (n_pages + pps - 1) / pps;
+  if (r.split >= r.n_splits) return false;
+  r.p0 = r.split * pps;
+  r.np = min(pps, n_pages - r.p0);
+  r.T = min(L, (r.p0 + r.np) * 16) - r.p0 * 16;
+  r.n_tiles = (r.np + 7) / 8;
+  return true;
+}
+
+template <int G>
+__global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
+    decode_tc_stream_kernel(const __grid_constant__ CUtensorMap map_k,
+                            const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q,
+                            const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+                            const int32_t* __restrict__ block_tables,
+                            const int32_t* __restrict__ seq_lens, float* __restrict__ out,
+                            float* __restrict__ ws_acc, float2* __restrict__ ws_ml, int num_seqs,
+                            int num_heads, int num_kv_heads, int64_t num_blocks,
+                            int max_blocks_per_seq, float qk_scale, int pages_per_split,
+                            int max_splits, int* err) {
+  using C = TcsCfg<G>;
+  constexpr int NQ = C::kNQ;
+  constexpr int BS = 16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* s_p = smem + C::kOffP;
+  float* s_logit = reinterpret_cast<float*>(smem + C::kOffLogit);
+  float* s_red = reinterpret_cast<float*>(smem + C::kOffRed);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffTmem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* meta_full = empty + C::kStages;
+  uint64_t* meta_free = meta_full + 2;
+  uint64_t* k_done = meta_free + 2;
+  uint64_t* d1_free = k_done + 1;
+  uint64_t* p_ready = d1_free + 1;
+  uint64_t* pv_done = p_ready + 1;
+  auto meta = [&](int b) { return smem + C::kOffMeta + b * C::kMetaBytes; };
+  auto qtile = [&](int b) { return smem + C::kOffQ + b * C::kRowBytes; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t n_units = (int64_t)num_seqs * num_kv_heads * max_splits;
+  const int64_t stride = gridDim.x;
+  if (tid == 0) {
+    if (blockIdx.x == 0)
+      for (int s = 0; s < num_seqs; ++s)
+        if (max(seq_lens[s], 0) > covered_pages(seq_lens[s], BS, max_blocks_per_seq) * BS)
+          record_error(err, kDevSeqTooLong);
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&meta_full[i], 2);  // the two table warps
+      mbar_init(&meta_free[i], 3);  // TMA warp, MMA lane (commit), epilogue
+    }
+    mbar_init(k_done, 1);
+    mbar_init(d1_free, 1);
+    mbar_init(p_ready, 1);
+    mbar_init(pv_done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(s_tmem, C::kTmemCols);
+  tmem_fence_before_sync();
+  __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 2 || warp == 3) {
+    // ---- chunk tables: warp 2 block ids / scales / counts, warp 3 query digits
+    TcsUnit un;
+    int k = 0;
+    for (int64_t u = blockIdx.x; u < n_units; u += stride) {
+      if (!tcs_unit(u, num_kv_heads, max_splits, pages_per_split, seq_lens, max_blocks_per_seq, un))
+        continue;
+      const int b = k & 1;
+      if (k >= 2) {
+        bool ok = true;
+        if (lane == 0 && !mbar_wait_bounded(&meta_free[b], (uint32_t)((k >> 1) - 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok = false;
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      uint8_t* m = meta(b);
+      if (warp == 2) {
+        int* phys_t = reinterpret_cast<int*>(m + C::kMetaPhys);
+        float* ks_t = reinterpret_cast<float*>(m + C::kMetaKs);
+        float* vs_t = reinterpret_cast<float*>(m + C::kMetaVs);
+        float vmax = 0.0f;
+        for (int pg = lane; pg < un.np; pg += 32) {
+          const int phys = block_tables[(int64_t)un.seq * max_blocks_per_seq + un.p0 + pg];
+          const bool okb = phys >= 0 && (int64_t)phys < num_blocks;
+          if (!okb) record_error(err, kDevBadBlockId);
+          phys_t[pg] = okb ? phys : -1;
+          const int64_t si = (int64_t)(okb ? phys : 0) * num_kv_heads + un.j;
+          ks_t[pg] = okb ? k_scale[si] : 0.0f;
+          const float vs = okb ? v_scale[si] : 0.0f;
+          vs_t[pg] = vs;
+          vmax = fmaxf(vmax, vs);
+        }
+        vmax = warp_max(vmax);
+        if (lane == 0) {
+          reinterpret_cast<int*>(m + C::kMetaT)[0] = un.T;
+          reinterpret_cast<float*>(m + C::kMetaT)[1] = vmax;
+        }
+      } else {
+        uint8_t* sq = qtile(b);
+        float* qs_t = reinterpret_cast<float*>(m + C::kMetaQs);
+        for (int g = 0; g < G; ++g) {
+          const float4 x = reinterpret_cast<const float4*>(
+              q + ((int64_t)un.seq * num_heads + (int64_t)un.j * G + g) * 128)[lane];
+          float mx = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+          mx = warp_max(mx);
+          const float inv = mx > 0.0f ? (float)kQFix / mx : 0.0f;
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+          int d[4][3];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            int n = __float2int_rn(xs[e] * inv);
+            n = max(-kQFix, min(kQFix, n));
+            to_digits(n, d[e][0], d[e][1], d[e][2]);
+          }
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl)
+            *reinterpret_cast<uint32_t*>(sq + sw128_offset(3 * g + pl, 4 * lane)) =
+                pack4(d[0][pl], d[1][pl], d[2][pl], d[3][pl]);
+          if (lane == 0) qs_t[g] = mx > 0.0f ? mx / (float)kQFix : 0.0f;
+        }
+        for (int r = 3 * G; r < NQ; ++r)
+          *reinterpret_cast<uint32_t*>(sq + sw128_offset(r, 4 * lane)) = 0u;
+        fence_proxy_async_smem();  // an MMA operand
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_full[b]);
+      ++k;
+    }
+  } else if (warp == 0) {
+    // ---- TMA: per unit its K tiles, then its V tiles ---------------------------
+    if (lane == 0) {
+      const uint64_t policy = l2_policy_evict_first();
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+      TcsUnit un;
+      int k = 0, ns = 0;
+      bool ok_run = true;
+      for (int64_t u = blockIdx.x; u < n_units && ok_run; u += stride) {
+        if (!tcs_unit(u, num_kv_heads, max_splits, pages_per_split, seq_lens, max_blocks_per_seq, un))
+          continue;
+        const int b = k & 1;
+        if (!mbar_wait_bounded(&meta_full[b], (uint32_t)(k >> 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          break;
+        }
+        const int* phys_t = reinterpret_cast<const int*>(meta(b) + C::kMetaPhys);
+        for (int kind = 0; kind < 2 && ok_run; ++kind) {
+          for (int ti = 0; ti < un.n_tiles; ++ti, ++ns) {
+            const int st = ns % C::kStages;
+            if (!mbar_wait_bounded(&empty[st], ((uint32_t)(ns / C::kStages) & 1u) ^ 1u, err)) {
+              record_error(err, kDevWaitTimeout);
+              ok_run = false;
+              break;
+            }
+            const int pb = ti * 8, pe = min(un.np, pb + 8);
+            mbar_arrive_expect_tx(&full[st], (uint32_t)((pe - pb) * BS * 128));
+            for (int pg = pb; pg < pe; ++pg)
+              tma_load_3d(smem + st * kStageBytes + (pg - pb) * BS * 128, kind ? &map_v : &map_k,
+                          &full[st], 0, un.j, max(phys_t[pg], 0) * BS, policy);
+          }
+        }
+        mbar_arrive(&meta_free[b]);
+        ++k;
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issue ---------------------------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t kIdQK = umma_i8_idesc(1, 1, 0, 0, 128, NQ);
+      constexpr uint32_t kIdPV = umma_i8_idesc(1, 0, 1, 0, 128, NQ);
+      const uint32_t stage0 = smem_u32(smem);
+      const uint32_t paddr = smem_u32(s_p);
+      TcsUnit un;
+      // this CTA's units and page tiles, for the reuse tests below
+      int total_units = 0, total_ns = 0;
+      for (int64_t u = blockIdx.x; u < n_units; u += stride)
+        if (tcs_unit(u, num_kv_heads, max_splits, pages_per_split, seq_lens, max_blocks_per_seq, un)) {
+          ++total_units;
+          total_ns += 2 * un.n_tiles;
+        }
+      int k = 0, ns = 0;
+      bool ok_run = true;
+      for (int64_t u = blockIdx.x; u < n_units && ok_run; u += stride) {
+        if (!tcs_unit(u, num_kv_heads, max_splits, pages_per_split, seq_lens, max_blocks_per_seq, un))
+          continue;
+        const int b = k & 1;
+        const uint32_t qaddr = smem_u32(qtile(b));
+        if (!mbar_wait_bounded(&meta_full[b], (uint32_t)(k >> 1) & 1u, err) ||
+            (k > 0 && !mbar_wait_bounded(d1_free, (uint32_t)(k - 1) & 1u, err))) {
+          record_error(err, kDevWaitTimeout);
+          break;
+        }
+        tmem_fence_after_sync();
+        for (int ti = 0; ti < un.n_tiles && ok_run; ++ti, ++ns) {
+          const int st = ns % C::kStages;
+          if (!mbar_wait_bounded(&full[st], (uint32_t)(ns / C::kStages) & 1u, err)) {
+            record_error(err, kDevWaitTimeout);
+            ok_run = false;
+            break;
+          }
+          tmem_fence_after_sync();
+          const uint32_t a = stage0 + st * kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8(tmem + ti * NQ, umma_sw128_desc(a + kk * 32, 16, 1024),
+                    umma_sw128_desc(qaddr + kk * 32, 16, 1024), kIdQK, kk > 0);
+          if (ns + C::kStages < total_ns) umma_commit(&empty[st]);
+        }
+        umma_commit(k_done);
+        if (k + 2 < total_units) umma_commit(&meta_free[b]);  // q digits read
+        if (ok_run && !mbar_wait_bounded(p_ready, (uint32_t)k & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok_run = false;
+        }
+        tmem_fence_after_sync();
+        for (int ti = 0; ti < un.n_tiles && ok_run; ++ti, ++ns) {
+          const int st = ns % C::kStages;
+          if (!mbar_wait_bounded(&full[st], (uint32_t)(ns / C::kStages) & 1u, err)) {
+            record_error(err, kDevWaitTimeout);
+            ok_run = false;
+            break;
+          }
+          tmem_fence_after_sync();
+          const uint32_t a = stage0 + st * kStageBytes;
+          const uint32_t pb = paddr + ti * C::kRowBytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8(tmem + C::kD2Col, umma_sw128_desc(a + kk * 4096, 16, 1024),
+                    umma_sw128_desc(pb + kk * 32, 16, 1024), kIdPV, (ti > 0 || kk > 0) ? 1u : 0u);
+          if (ns + C::kStages < total_ns) umma_commit(&empty[st]);
+        }
+        umma_commit(pv_done);
+        ++k;
+      }
+    }
+  } else {
+    // ---- epilogue: logits, softmax, probability planes, output ------------------
+    const int w4 = warp - 4;
+    const int e = tid - 128;
+    const uint32_t lane_base = (uint32_t)(32 * w4) << 16;
+    float* red_m = s_red;
+    float* red_l = s_red + 32;
+    TcsUnit un;
+    int k = 0;
+    bool live = true;
+    for (int64_t u = blockIdx.x; u < n_units; u += stride) {
+      if (!tcs_unit(u, num_kv_heads, max_splits, pages_per_split, seq_lens, max_blocks_per_seq, un))
+        continue;
+      const int b = k & 1;
+      const uint8_t* m = meta(b);
+      const int* phys_t = reinterpret_cast<const int*>(m + C::kMetaPhys);
+      const float* ks_t = reinterpret_cast<const float*>(m + C::kMetaKs);
+      const float* vs_t = reinterpret_cast<const float*>(m + C::kMetaVs);
+      const float* qs_t = reinterpret_cast<const float*>(m + C::kMetaQs);
+      if (live && (!mbar_wait_bounded(&meta_full[b], (uint32_t)(k >> 1) & 1u, err) ||
+                   !mbar_wait_bounded(k_done, (uint32_t)k & 1u, err))) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
+      }
+      tmem_fence_after_sync();
+      const int T = un.T;
+      const float vmax = reinterpret_cast<const float*>(m + C::kMetaT)[1];
+      float kmax[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) kmax[g] = -INFINITY;
+      for (int ti = 0; ti < un.n_tiles; ++ti) {
+        const int tok = ti * C::kTileTok + e;
+        const int pg = min(tok / BS, C::kMaxPages - 1);
+        const bool valid = live && tok < T && phys_t[pg] >= 0;
+        const float ks = ks_t[pg];
+        tmem_row_groups<G, NQ>(tmem + lane_base + ti * NQ, [&](int g, float v) {
+          const float logit = valid ? v * (qs_t[g] * ks * qk_scale) : -INFINITY;
+          s_logit[g * C::kMaxTok + tok] = logit;
+          kmax[g] = fmaxf(kmax[g], logit);
+        });
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float mm = warp_max(kmax[g]);
+        if (lane == 0) red_m[w4 * 8 + g] = mm;
+      }
+      tmem_fence_before_sync();
+      named_barrier(1, 128);  // maxima published; D1 read by all four warps
+      if (e == 0) mbar_arrive(d1_free);
+      const float to_fix = vmax > 0.0f ? 16777215.0f / vmax : 0.0f;
+      float mh[G], l[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        mh[g] = fmaxf(fmaxf(red_m[g], red_m[8 + g]), fmaxf(red_m[16 + g], red_m[24 + g]));
+        l[g] = 0.0f;
+      }
+      for (int ti = 0; ti < un.n_tiles; ++ti) {
+        const int tok = ti * C::kTileTok + e;
+        const float vs = vs_t[min(tok / BS, C::kMaxPages - 1)];
+        uint8_t* pt = s_p + ti * C::kRowBytes;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          uint32_t n = 0;
+          if (tok < T && mh[g] != -INFINITY) {
+            const float p = exp2f(s_logit[g * C::kMaxTok + tok] - mh[g]);
+            l[g] += p;
+            n = __float2uint_rn(fminf(p * vs * to_fix, 16777215.0f));
+          }
+          pt[sw128_offset(3 * g, e)] = (uint8_t)(n & 255u);
+          pt[sw128_offset(3 * g + 1, e)] = (uint8_t)((n >> 8) & 255u);
+          pt[sw128_offset(3 * g + 2, e)] = (uint8_t)(n >> 16);
+        }
+        for (int rw = 3 * G; rw < NQ; ++rw) pt[sw128_offset(rw, e)] = 0;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float s = warp_sum(l[g]);
+        if (lane == 0) red_l[w4 * 8 + g] = s;
+      }
+      fence_proxy_async_smem();
+      named_barrier(1, 128);
+      if (e == 0) {
+        mbar_arrive(p_ready);
+        mbar_arrive(&meta_free[b]);  // the epilogue is done with this table half
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        l[g] = (red_l[g] + red_l[8 + g]) + (red_l[16 + g] + red_l[24 + g]);
+      if (live && !mbar_wait_bounded(pv_done, (uint32_t)k & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
+      }
+      tmem_fence_after_sync();
+      const float back = vmax * (1.0f / 16777215.0f);
+      tmem_row_groups<G, NQ>(tmem + lane_base + C::kD2Col, [&](int g, float v) {
+        const float acc = v * back;
+        const int hq = un.j * G + g;
+        if (un.n_splits == 1) {
+          out[((int64_t)un.seq * num_heads + hq) * 128 + e] = l[g] > 0.0f ? acc / l[g] : 0.0f;
+        } else {
+          const int64_t slot = ((int64_t)un.seq * max_splits + un.split) * num_heads + hq;
+          ws_acc[slot * 128 + e] = acc;
+          if (e == 0) ws_ml[slot] = make_float2(mh[g], l[g]);
+        }
+      });
+      tmem_fence_before_sync();
+      // every epilogue thread has read D2 before the next unit's p_ready
+      // (which lets the MMA lane overwrite it) -- the first named barrier of
+      // the next unit orders that
+      ++k;
+    }
+  }
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
 // ===========================================================================
 // Planning and dispatch
 // ===========================================================================
@@ -1990,6 +2433,19 @@ int launch_tc_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_ml
       !cached_cache_map(&mv, a.v_cache, a.num_blocks, 16, a.num_kv_heads, 1)) {
     set_error("cuTensorMapEncodeTiled failed for the paged cache");
     return kCudaError;
+  }
+  if (env_int("PKV_DECODE_TC_SPLIT", 0) == 0) {  // persistent form
+    using CS = TcsCfg<G>;
+    auto skern = decode_tc_stream_kernel<G>;
+    cudaFuncSetAttribute(skern, cudaFuncAttributeMaxDynamicSharedMemorySize, CS::kSmemBytes);
+    const int64_t units = (int64_t)a.num_seqs * a.num_kv_heads * p.max_splits;
+    const int64_t ctas = std::max<int64_t>(
+        1, std::min<int64_t>(units, (int64_t)CS::kMinBlocks * sm_count()));
+    skern<<<(unsigned)ctas, CS::kThreads, CS::kSmemBytes, stream>>>(
+        mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out, ws_acc, ws_ml,
+        a.num_seqs, a.num_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq,
+        a.sm_scale * kLog2e, p.pages_per_split, p.max_splits, device_error_word());
+    return kOk;
   }
   auto kern = decode_tc_kernel<G>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
