@@ -353,7 +353,8 @@ __global__ void __launch_bounds__(kFastThreads, 2)
       prefetch_tensormap(&map_v);
       const uint64_t policy = l2_policy_evict_first();
       const int total = 2 * n_stages;
-      for (int i = 0; i < total; ++i) {
+      int i = 0;
+      for (; i < total; ++i) {
         const int slot = i % kFastStages;
         const uint32_t ph = (uint32_t)(i / kFastStages) & 1u;
         if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, err)) {
@@ -371,6 +372,7 @@ __global__ void __launch_bounds__(kFastThreads, 2)
                       is_v ? &map_v : &map_k, &full[slot], 0, j0, phys * BS, policy);
         }
       }
+      drain_ring(full, kFastStages, i);  // no copy outlives the CTA
     }
     return;
   }
@@ -907,22 +909,25 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       publish(0, c0, true, p0, ks0, vs0);
       if (have1) publish(1, c1, c1.s != c0.s || c1.g != c0.g, p1, ks1, vs1);
     }
-    if (!have1) return;
-    StreamChunk prev = c1, cur;
-    for (int i = 2; it.next(cur); ++i) {
-      const int b = i & 1;
-      bool ok = true;
-      if (lane == 0 && !mbar_wait_bounded(&chunk_free[b], (uint32_t)((i >> 1) - 1) & 1u, err)) {
-        record_error(err, kDevWaitTimeout);
-        ok = false;
+    int published = have1 ? 2 : 1;
+    if (have1) {
+      StreamChunk prev = c1, cur;
+      for (; it.next(cur); ++published) {
+        const int i = published, b = i & 1;
+        bool ok = true;
+        if (lane == 0 && !mbar_wait_bounded(&chunk_free[b], (uint32_t)((i >> 1) - 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok = false;
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        float ks[HG], vs[HG];
+        const int ph = load_phys(cur);
+        load_scales(cur, ph, ks, vs);
+        publish(b, cur, cur.s != prev.s || cur.g != prev.g, ph, ks, vs);
+        prev = cur;
       }
-      if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-      float ks[HG], vs[HG];
-      const int ph = load_phys(cur);
-      load_scales(cur, ph, ks, vs);
-      publish(b, cur, cur.s != prev.s || cur.g != prev.g, ph, ks, vs);
-      prev = cur;
     }
+    if (lane == 0) drain_ring(meta_full, 2, published);  // the q-row copies have landed
     return;
   }
 
@@ -964,6 +969,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
         if (!ok_run) break;
         mbar_arrive(&chunk_free[b]);  // this warp is done with the chunk's table
       }
+      drain_ring(full, kFastStages, ns);  // no copy outlives the CTA
     }
     return;
   }
@@ -1690,6 +1696,7 @@ __global__ void __launch_bounds__(256, TcCfg<G>::kMinBlocks)
                         &full[st], 0, j, max(s_phys[pg], 0) * BS, policy);
         }
       }
+      drain_ring(full, C::kStages, ns);  // no copy outlives the CTA
     }
   } else if (warp == 1) {
     // ---- MMA issue: one thread ---------------------------------------------
@@ -1742,6 +1749,7 @@ __global__ void __launch_bounds__(256, TcCfg<G>::kMinBlocks)
         if (ns + C::kStages < 2 * n_tiles) umma_commit(&empty[st]);
       }
       umma_commit(pv_done);  // the last arrival: the epilogue waits for it
+      mbar_drain(pv_done, 0);  // every MMA of this thread is done before TMEM is freed
     }
   } else if (warp >= 4) {
     // ---- logits, softmax, probability planes, output -----------------------
@@ -2081,6 +2089,7 @@ __global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
         mbar_arrive(&meta_free[b]);
         ++k;
       }
+      drain_ring(full, C::kStages, ns);  // no copy outlives the CTA
     }
   } else if (warp == 1) {
     // ---- MMA issue ---------------------------------------------------------
@@ -2151,6 +2160,8 @@ __global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
         umma_commit(pv_done);
         ++k;
       }
+      // every MMA of this thread is done before TMEM is freed
+      if (k > 0) mbar_drain(pv_done, (uint32_t)(k - 1) & 1u);
     }
   } else {
     // ---- epilogue: logits, softmax, probability planes, output ------------------

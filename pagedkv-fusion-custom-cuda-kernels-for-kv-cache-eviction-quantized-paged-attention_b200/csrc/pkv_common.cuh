@@ -143,6 +143,27 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Waits (at most limit_ns, ignoring the error word) for the phase of a
+// barrier that this thread's own copies complete: a producer calls it for
+// every load it issued before it exits, so that no copy can land in shared
+// memory after the CTA is gone -- also on an error path, where the
+// consumers stopped waiting.  Copies complete on their own, so this ends
+// promptly.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity,
+                                           uint64_t limit_ns = 200000000ull) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait_suspend(bar, parity, 100000u))
+    if (global_timer_ns() - t0 > limit_ns) return;
+}
+
+// Drains the last min(issued, stages) loads of a ring of `stages` full
+// barriers, load n having used stage n % stages in phase n / stages.
+__device__ __forceinline__ void drain_ring(uint64_t* full, int stages, int issued) {
+  for (int n = issued > stages ? issued - stages : 0; n < issued; ++n)
+    mbar_drain(&full[n % stages], (uint32_t)(n / stages) & 1u);
+}
+
 // ---------------------------------------------------------------------------
 // TMA: 3-D tiled bulk-tensor load into this CTA's shared memory.  No
 // multicast: every copy reads this GPU's own global memory only.

@@ -225,15 +225,19 @@ __global__ void __launch_bounds__(kQThreads)
 // head_dim 128, 16-token blocks of at most kBulkMaxBlock bytes (fp16/bf16
 // with <= 9 KV heads, fp32 with <= 4): a persistent kernel streams whole
 // blocks (contiguous in the [NB, bs, Hkv, D] layout) into a ring of shared
-// memory stages with one cp.async.bulk each.  Sixteen consumer warps take
-// every block together, two per head (8 tokens each): absmax of the half,
-// exchange through shared memory, codes.  Every consumer warp passes every
-// stage phase in order -- a warp that skipped blocks could wait on a
-// stage's next phase while the current one is incomplete and, the parities
-// of phases k-1 and k+1 being equal, pass it early.  Deep queues with few
-// registers: the register kernel above keeps one block-head in flight per
-// warp and its CTAs turn over every few microseconds.
-constexpr int kBulkConsumerWarps = 16;
+// memory stages with one cp.async.bulk each.  The 16 consumer warps take the
+// blocks two at a time: every warp waits for both blocks of a pair -- so
+// every warp passes every stage phase in order (a warp that skipped blocks
+// could wait on a stage's next phase while the current one is incomplete
+// and, the parities of phases k-1 and k+1 being equal, pass it early) --
+// then warps 0-7 quantize the first block and warps 8-15 the second, one
+// head per warp.  A stage is refilled only after all 16 warps released it
+// (those not quantizing it right after their wait), so no warp can still be
+// waiting on a phase of a stage that has moved on.  Deep queues with few registers: the register kernel above
+// keeps one block-head in flight per warp and its CTAs turn over every few
+// microseconds.
+constexpr int kBulkHalfWarps = 8;
+constexpr int kBulkConsumerWarps = 2 * kBulkHalfWarps;
 constexpr int kBulkThreads = kBulkConsumerWarps * 32 + 32;
 constexpr uint32_t kBulkMaxBlock = 36 * 1024;
 constexpr int kBulkMaxHeads = 9;
@@ -313,7 +317,6 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
   const uint32_t block_bytes = (uint32_t)(elems * sizeof(T));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kBulkStages * block_bytes);
   uint64_t* empty = full + kBulkStages;
-  uint32_t* s_half = reinterpret_cast<uint32_t*>(empty + kBulkStages);  // [2][heads][2]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < kBulkStages; ++i) {
@@ -339,58 +342,68 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
         bulk_load_g2s(smem_raw + st * block_bytes, kv + b * elems, block_bytes, &full[st]);
         ++n;
       }
+      drain_ring(full, kBulkStages, n);  // no copy outlives this warp
     }
     return;
   }
 
-  const int h0 = warp % 8;      // heads h0, h0 + 8
-  const int half = warp / 8;    // tokens [8 * half, 8 * half + 8)
+  const int half = warp / kBulkHalfWarps;  // which block of the pair
+  const int h0 = warp % kBulkHalfWarps;    // heads h0, h0 + 8
   const int64_t tok = (int64_t)hkv * 128;
   bool live = true;
-  int n = 0;
-  for (int64_t b = blockIdx.x; b < nb; b += gridDim.x) {
-    if (skip != nullptr && skip[b]) continue;
-    const int st = n % kBulkStages;
-    const uint32_t ph = (uint32_t)(n / kBulkStages) & 1u;
-    uint32_t* amax_buf = s_half + (n & 1) * kBulkMaxHeads * 2;
-    ++n;
-    if (live && !mbar_wait_bounded(&full[st], ph, err)) {
-      record_error(err, kDevWaitTimeout);
-      live = false;
-    }
-    const T* blk = reinterpret_cast<const T*>(smem_raw + st * block_bytes);
-    if (live) {
-      for (int h = h0; h < hkv; h += 8) {
-        const T* row0 = blk + (int64_t)(8 * half) * tok + (int64_t)h * 128 + lane * 4;
-        uint32_t m = absmax_bits4<T>(row0);
-#pragma unroll
-        for (int t = 1; t < 8; ++t) m = absmax_fold<T>(m, absmax_bits4<T>(row0 + t * tok));
-        m = __reduce_max_sync(0xffffffffu, absmax_float_bits<T>(m));  // NaN wins
-        if (lane == 0) amax_buf[h * 2 + half] = m;
+  int n = 0;  // blocks of this CTA consumed so far (skipped ones excluded)
+  int64_t b = blockIdx.x;
+  for (;;) {
+    int64_t first = 0, second = 0;
+    int cnt = 0;
+    for (; cnt < 2 && b < nb; b += gridDim.x)
+      if (skip == nullptr || !skip[b]) {
+        if (cnt == 0) first = b; else second = b;
+        ++cnt;
+      }
+    if (cnt == 0) break;
+    for (int i = 0; i < cnt; ++i) {  // every warp passes both phases, in order
+      const int st = (n + i) % kBulkStages;
+      if (live && !mbar_wait_bounded(&full[st], (uint32_t)((n + i) / kBulkStages) & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
       }
     }
-    // both halves of every head published (amax_buf alternates per block, so
-    // this one barrier also keeps the next block from overwriting it early)
-    named_barrier(1, kBulkConsumerWarps * 32);
-    if (live) {
-      for (int h = h0; h < hkv; h += 8) {
-        const float amax = __uint_as_float(max(amax_buf[h * 2], amax_buf[h * 2 + 1]));
-        const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
-        if (lane == 0 && half == 0) scale[b * hkv + h] = s;
-        const float rcp = __frcp_rn(s);
-        const bool fast = isfinite(amax) && !isinf(rcp);
-        const T* row0 = blk + (int64_t)(8 * half) * tok + (int64_t)h * 128 + lane * 4;
-        int8_t* out = q + b * elems + (int64_t)(8 * half) * tok + (int64_t)h * 128 + lane * 4;
+    // the other block of the pair is released at once by the warps not quantizing it
+    if (cnt == 2 || half == 1) {
+      const int other = cnt == 2 ? (n + (half ^ 1)) % kBulkStages : n % kBulkStages;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[other]);
+    }
+    if (half < cnt) {
+      const int st = (n + half) % kBulkStages;
+      const int64_t blk_id = half ? second : first;
+      const T* blk = reinterpret_cast<const T*>(smem_raw + st * block_bytes);
+      if (live) {
+        for (int h = h0; h < hkv; h += kBulkHalfWarps) {
+          const T* row0 = blk + (int64_t)h * 128 + lane * 4;
+          uint32_t m = absmax_bits4<T>(row0);
+#pragma unroll 5
+          for (int t = 1; t < BS; ++t) m = absmax_fold<T>(m, absmax_bits4<T>(row0 + t * tok));
+          m = __reduce_max_sync(0xffffffffu, absmax_float_bits<T>(m));  // NaN wins
+          const float amax = __uint_as_float(m);
+          const float sc = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+          if (lane == 0) scale[blk_id * hkv + h] = sc;
+          const float rcp = __frcp_rn(sc);
+          const bool fast = isfinite(amax) && !isinf(rcp);
+          int8_t* out = q + blk_id * elems + (int64_t)h * 128 + lane * 4;
 #pragma unroll 2
-        for (int t = 0; t < 8; ++t) {
-          float f[4];
-          load4_shared<T>(row0 + t * tok, f);
-          *reinterpret_cast<uint32_t*>(out + t * tok) = quantize_word(f, s, rcp, fast);
+          for (int t = 0; t < BS; ++t) {
+            float f[4];
+            load4_shared<T>(row0 + t * tok, f);
+            *reinterpret_cast<uint32_t*>(out + t * tok) = quantize_word(f, sc, rcp, fast);
+          }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
+    n += cnt;
   }
 }
 
@@ -410,8 +423,7 @@ int launch_quantize_t(const T* kv, int8_t* q, float* scale, int64_t nb, int bs, 
   if (hd == 128 && bs == 16 && block_bytes <= kBulkMaxBlock && hkv <= kBulkMaxHeads &&
       reinterpret_cast<uintptr_t>(kv) % 16 == 0 && reinterpret_cast<uintptr_t>(q) % 4 == 0 &&
       std::getenv("PKV_QUANTIZE_REGISTER") == nullptr) {
-    const size_t smem = kBulkStages * block_bytes + 2 * kBulkStages * sizeof(uint64_t) +
-                        2 * kBulkMaxHeads * 2 * sizeof(uint32_t);
+    const size_t smem = kBulkStages * block_bytes + 2 * kBulkStages * sizeof(uint64_t);
     auto kern = quantize_bulk_kernel<T>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t ctas = std::min<int64_t>(nb, 2LL * sm_count_quant());
