@@ -209,7 +209,8 @@ int pkv_compact_block_tables(const int32_t *block_tables,
  * Envelope: head_dim % 32 == 0 and <= 256, block_size <= 64,
  * num_heads % num_kv_heads == 0.  The workspace holds the partial results
  * of sequences whose pages are split across CTAs, and one arrival counter
- * per (sequence, KV-head group) that the call resets on its stream.
+ * per (sequence, KV-head group); it needs no initialisation (the counters
+ * carry a per-launch tag) and the call issues no memset.
  */
 size_t pkv_quant_paged_attention_workspace_size(
     int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,

@@ -31,10 +31,12 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <random>
 
 #include "pkv_common.cuh"
 #include "pkv_internal.h"
@@ -610,9 +612,12 @@ __global__ void __launch_bounds__(kFastThreads, 2)
 // leaves one partial (acc, m, l) per CTA at slot unit + c; the CTA whose
 // arrival on the unit's counter completes the set merges them in segment
 // order (so the result does not depend on which CTA arrives last) and
-// writes the output.  The counters are zeroed on the stream before launch.
+// writes the output.  The counters carry a per-launch tag (arrive_on_unit),
+// so no memset precedes the launch.  A small batch (fewer than min_pages
+// pages per CTA of the grid) is spread over fewer CTAs.
 
 constexpr int kStreamMaxSeqs = 1024;
+constexpr int kMergeDepth = 2;  // partial rows in flight per merging warp
 constexpr int kStreamThreads = kConsumers + 64;  // + TMA warp + table warp
 constexpr int kTmaWarp = kConsumerWarps;
 constexpr int kTableWarp = kConsumerWarps + 1;
@@ -739,6 +744,36 @@ __device__ __forceinline__ bool cta_owns_pages(long long P, int c, int C) {
   return P * c / C < P * (c + 1) / C;
 }
 
+// Arrival counters need no reset before a launch.  A counter holds
+// (launch tag << kArrivalBits) | arrivals.  At kernel start the CTA that owns
+// the first page of a split unit stamps the unit's counter with this
+// launch's tag and a count of 0 (stamp_unit); the unit's CTAs then arrive
+// with one atomic add each, and the arrival that completes the set writes 0
+// back, so a CUDA-graph replay of the same launch (same tag) finds no stale
+// tag either.  An arrival that finds another tag came before the stamp (its
+// CTA finished before the unit's first CTA started): the stamp overwrites
+// its add, so it waits for the stamp (bounded) and adds again.  Returns 1
+// for the completing arrival, 0 otherwise, -1 when the stamp never came.
+constexpr int kArrivalBits = 20;
+__device__ __forceinline__ void stamp_unit(unsigned long long* ctr, unsigned long long tag) {
+  *reinterpret_cast<volatile unsigned long long*>(ctr) = tag << kArrivalBits;
+}
+__device__ __forceinline__ int arrive_on_unit(unsigned long long* ctr, unsigned long long tag,
+                                              int nseg) {
+  constexpr unsigned long long kCount = (1ull << kArrivalBits) - 1;
+  for (;;) {
+    const unsigned long long old = atomic_add_acq_rel_gpu_u64(ctr, 1ull);
+    if ((old >> kArrivalBits) == tag) {
+      const bool last = (int)(old & kCount) + 1 == nseg;
+      if (last) *reinterpret_cast<volatile unsigned long long*>(ctr) = 0ull;
+      return last ? 1 : 0;
+    }
+    const uint64_t t0 = global_timer_ns();
+    while ((*reinterpret_cast<volatile unsigned long long*>(ctr) >> kArrivalBits) != tag)
+      if (global_timer_ns() - t0 > 2000000000ull) return -1;
+  }
+}
+
 template <int BS, int HG, int G>
 __global__ void __launch_bounds__(kStreamThreads, 2)
     decode_stream_kernel(const __grid_constant__ CUtensorMap map_k,
@@ -747,9 +782,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
                          const int32_t* __restrict__ block_tables,
                          const int32_t* __restrict__ seq_lens, float* __restrict__ out,
                          float* __restrict__ ws_acc, float2* __restrict__ ws_ml,
-                         int* __restrict__ unit_arrivals, int num_seqs, int num_heads,
+                         unsigned long long* __restrict__ unit_arrivals, int num_seqs, int num_heads,
                          int num_kv_heads, int64_t num_blocks, int max_blocks_per_seq,
-                         float qk_scale, int* err) {
+                         float qk_scale, int min_pages, unsigned long long launch_tag,
+                         int* err) {
   using F = FastCfg<BS, HG, G>;
   using C = StreamCfg<BS, HG, G>;
   extern __shared__ uint8_t smem_raw[];
@@ -773,7 +809,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
   const int lane = tid & 31;
   const int S = num_seqs;
   const int ng = num_kv_heads / HG;
-  const int n_ctas = gridDim.x;
+  const int grid_ctas = gridDim.x;
 
   // ---- pages per sequence and their prefix (every CTA, identically) -------
   constexpr int kPer = (kStreamMaxSeqs + kStreamThreads - 1) / kStreamThreads;
@@ -821,12 +857,16 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
   }
   __syncthreads();
   // sequences without pages: zero output (no unit covers them)
-  for (int s = blockIdx.x; s < S; s += n_ctas) {
+  for (int s = blockIdx.x; s < S; s += grid_ctas) {
     if (s_pseq[s + 1] != s_pseq[s]) continue;
     float4* o = reinterpret_cast<float4*>(out + (int64_t)s * num_heads * 128);
     for (int i = tid; i < num_heads * 32; i += kStreamThreads) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const long long P = (long long)s_pseq[S] * ng;
+  // a small batch goes to fewer CTAs, at least min_pages pages each, so that
+  // a unit leaves few partials to merge (every CTA derives the same count)
+  const int n_ctas = (int)min((long long)grid_ctas, max(1LL, (P + min_pages - 1) / min_pages));
+  if (blockIdx.x >= n_ctas) return;  // uniform
   const long long c_begin = P * blockIdx.x / n_ctas;
   const long long c_end = P * (blockIdx.x + 1) / n_ctas;
   if (c_begin >= c_end) return;  // uniform
@@ -937,6 +977,13 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       const uint64_t policy = l2_policy_evict_first();
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
+      {  // while the first table loads: stamp the counters of the split units
+         // whose first page is here
+        StreamIter w = it;
+        StreamChunk c;
+        while (w.next(c))
+          if (c.lp0 == 0 && !c.whole) stamp_unit(&unit_arrivals[c.s * ng + c.g], launch_tag);
+      }
       int ns = 0;
       for (int i = 0; it.next(ch); ++i) {
         const int b = i & 1;
@@ -1259,7 +1306,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
                 make_float4(acc_run[g][0], acc_run[g][1], acc_run[g][2], acc_run[g][3]);
             if (lane == 0) ws_ml[slot] = s_run[hg];
           }
-          __threadfence();
         }
         // the unit's CTAs, in page order
         const int pages = s_pseq[ch.s + 1] - s_pseq[ch.s];
@@ -1267,52 +1313,61 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
         const int first = page_owner(ustart, P, n_ctas);
         const int last = page_owner(ustart + pages - 1, P, n_ctas);
         const bool all_own = P >= n_ctas;  // then every CTA owns >= 1 page
+        // every partial store of this CTA is ordered before thread 0's
+        // release by the barrier; the last arrival acquires all of them
         named_barrier(1, kConsumers);
         if (tid == 0) {
-          int nseg = last - first + 1;
-          if (!all_own) {
-            nseg = 0;
-            for (int c = first; c <= last; ++c) nseg += cta_owns_pages(P, c, n_ctas);
-          }
-          const int done = atomicAdd(&unit_arrivals[u], 1) + 1;
-          s_tmp[32] = done == nseg;
+          // with fewer pages than CTAs every CTA owns at most one page, so
+          // the unit's pages have distinct owners; otherwise every CTA in
+          // [first, last] owns some
+          const int nseg = all_own ? last - first + 1 : pages;
+          const int r = arrive_on_unit(&unit_arrivals[u], launch_tag, nseg);
+          if (r < 0) record_error(err, kDevWaitTimeout);
+          s_tmp[32] = r == 1;
         }
         named_barrier(1, kConsumers);
         if (s_tmp[32] && v_r == 0) {  // this CTA completed the set: merge
-          __threadfence();
 #pragma unroll 1
           for (int g = 0; g < F::kGPW; ++g) {
             const int hg = v_jj * G + g0 + g;
             auto slot_of = [&](int c) { return ((int64_t)u + c) * F::kNHG + hg; };
-            float M = -INFINITY;
-            for (int b = first; b <= last; b += 32) {
-              const int c = b + lane;
-              if (c <= last && (all_own || cta_owns_pages(P, c, n_ctas)))
-                M = fmaxf(M, __ldcg(&ws_ml[slot_of(c)]).x);
-            }
+            // (m, l) of this lane's CTA; the first 32 are kept for the second pass
+            auto load_ml = [&](int c) {
+              return c <= last && (all_own || cta_owns_pages(P, c, n_ctas))
+                         ? __ldcg(&ws_ml[slot_of(c)])
+                         : make_float2(-INFINITY, 0.0f);
+            };
+            const float2 ml0 = load_ml(first + lane);
+            float M = ml0.x;
+            for (int b = first + 32; b <= last; b += 32) M = fmaxf(M, load_ml(b + lane).x);
             M = warp_max(M);
             float den = 0.0f;
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int b = first; b <= last; b += 32) {
-              const int c = b + lane;
+              const float2 ml = b == first ? ml0 : load_ml(b + lane);
               float w = 0.0f;
-              if (c <= last && (all_own || cta_owns_pages(P, c, n_ctas))) {
-                const float2 ml = __ldcg(&ws_ml[slot_of(c)]);
-                if (ml.x != -INFINITY) {
-                  w = exp2f(ml.x - M);
-                  den += w * ml.y;
-                }
+              if (ml.x != -INFINITY) {
+                w = exp2f(ml.x - M);
+                den += w * ml.y;
               }
               const int nb = min(32, last - b + 1);
-#pragma unroll 4
-              for (int j = 0; j < nb; ++j) {
-                const float wj = __shfl_sync(0xffffffffu, w, j);
-                if (wj != 0.0f) {
-                  const float4 x = __ldcg(reinterpret_cast<const float4*>(ws_acc + slot_of(b + j) * 128) + lane);
-                  a.x += wj * x.x;
-                  a.y += wj * x.y;
-                  a.z += wj * x.z;
-                  a.w += wj * x.w;
+              // kMergeDepth partial rows in flight at a time; rows of CTAs that
+              // own no page of the unit (weight 0) are read but not added
+              for (int j0 = 0; j0 < nb; j0 += kMergeDepth) {
+                float4 x[kMergeDepth];
+#pragma unroll
+                for (int jj = 0; jj < kMergeDepth; ++jj)
+                  x[jj] = __ldcg(reinterpret_cast<const float4*>(
+                                     ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * 128) + lane);
+#pragma unroll
+                for (int jj = 0; jj < kMergeDepth; ++jj) {
+                  const float wj = __shfl_sync(0xffffffffu, w, (j0 + jj) & 31);
+                  if (j0 + jj < nb && wj != 0.0f) {
+                    a.x += wj * x[jj].x;
+                    a.y += wj * x[jj].y;
+                    a.z += wj * x[jj].z;
+                    a.w += wj * x[jj].w;
+                  }
                 }
               }
             }
@@ -1436,38 +1491,89 @@ __global__ void __launch_bounds__(kGenThreads)
 // Combine
 // ===========================================================================
 
-__global__ void __launch_bounds__(128)
+constexpr int kCombineThreads = 128;
+constexpr int kCombineChunk = 1024;  // split weights staged in shared memory at a time
+
+__device__ __forceinline__ float block_max_128(float v, float* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+}
+__device__ __forceinline__ float block_sum_128(float v, float* red) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+// One CTA per (sequence, query head).  Latency-bound: the splits' (m, l)
+// are read by all threads at once, and each output channel keeps eight
+// partial rows in flight; accumulation runs in split order.
+__global__ void __launch_bounds__(kCombineThreads)
     decode_combine_kernel(const int32_t* __restrict__ seq_lens, const float* __restrict__ ws_acc,
                           const float2* __restrict__ ws_ml, float* __restrict__ out,
                           int num_heads, int head_dim, int bs, int max_blocks_per_seq,
                           int pages_per_split, int max_splits) {
+  __shared__ float s_w[kCombineChunk];
+  __shared__ float s_red[kCombineThreads / 32];
   const int seq = blockIdx.x;
   const int h = blockIdx.y;
+  const int tid = threadIdx.x;
   const int n_pages = covered_pages(seq_lens[seq], bs, max_blocks_per_seq);
   const int n_splits = (n_pages + pages_per_split - 1) / pages_per_split;
   float* o = out + ((int64_t)seq * num_heads + h) * head_dim;
   if (n_splits == 0) {
-    for (int d = threadIdx.x; d < head_dim; d += blockDim.x) o[d] = 0.0f;
+    for (int d = tid; d < head_dim; d += kCombineThreads) o[d] = 0.0f;
     return;
   }
   if (n_splits == 1) return;  // written by the split kernel
   const int64_t base = (int64_t)seq * max_splits * num_heads + h;
   float M = -INFINITY;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, ws_ml[base + (int64_t)s * num_heads].x);
-  float denom = 0.0f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float2 ml = ws_ml[base + (int64_t)s * num_heads];
-    if (ml.x != -INFINITY) denom += exp2f(ml.x - M) * ml.y;
-  }
-  const float inv = denom > 0.0f ? 1.0f / denom : 0.0f;
-  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int s = 0; s < n_splits; ++s) {
-      const int64_t slot = base + (int64_t)s * num_heads;
-      const float mx = ws_ml[slot].x;
-      if (mx != -INFINITY) acc += exp2f(mx - M) * ws_acc[slot * head_dim + d];
+  for (int s = tid; s < n_splits; s += kCombineThreads)
+    M = fmaxf(M, __ldcg(&ws_ml[base + (int64_t)s * num_heads]).x);
+  M = block_max_128(M, s_red);
+  const int64_t stride = (int64_t)num_heads * head_dim;  // between splits of one head
+  float den = 0.0f;
+  float acc[2] = {0.0f, 0.0f};  // channels tid and tid + 128 (head_dim <= 256)
+  for (int c0 = 0; c0 < n_splits; c0 += kCombineChunk) {
+    const int cnt = min(kCombineChunk, n_splits - c0);
+    __syncthreads();  // the previous chunk's weights are consumed
+    for (int s = tid; s < cnt; s += kCombineThreads) {
+      const float2 ml = __ldcg(&ws_ml[base + (int64_t)(c0 + s) * num_heads]);
+      const float w = ml.x != -INFINITY ? exp2f(ml.x - M) : 0.0f;
+      s_w[s] = w;
+      den += w * ml.y;
     }
-    o[d] = acc * inv;
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int d = tid + r * kCombineThreads;
+      if (d < head_dim) {
+        const float* col = ws_acc + (base + (int64_t)c0 * num_heads) * head_dim + d;
+        float a = acc[r];
+        for (int s0 = 0; s0 < cnt; s0 += 8) {
+          float x[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = __ldcg(col + (int64_t)min(s0 + j, cnt - 1) * stride);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float w = s0 + j < cnt ? s_w[s0 + j] : 0.0f;
+            if (w != 0.0f) a += w * x[j];  // rows of empty splits are not added
+          }
+        }
+        acc[r] = a;
+      }
+    }
+  }
+  den = block_sum_128(den, s_red);
+  const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int d = tid + r * kCombineThreads;
+    if (d < head_dim) o[d] = acc[r] * inv;
   }
 }
 
@@ -2291,7 +2397,8 @@ struct Plan {
   int hg = 1, g = 1;
   int pages_per_split = 1;
   int max_splits = 1;
-  int n_ctas = 0;  // stream kernel grid
+  int n_ctas = 0;     // stream kernel grid
+  int min_pages = 1;  // stream kernel: fewest pages a CTA takes
 };
 
 int sm_count() {
@@ -2373,8 +2480,24 @@ Plan make_plan(const DecodeArgs& a) {
     p.stream = true;
     const int forced = env_int("PKV_DECODE_CTAS", 0);
     p.n_ctas = forced > 0 ? forced : 2 * sm_count();
+    p.min_pages = std::max(1, env_int("PKV_STREAM_MIN_PAGES", 4));
   }
   return p;
+}
+
+// A fresh tag per stream-kernel launch for its arrival counters: 44 bits
+// (the counters keep 20 for the count), never 0, starting at a random point
+// so that counters another process left behind do not match.
+unsigned long long next_launch_tag() {
+  static std::atomic<unsigned long long> tag{[] {
+    std::random_device rd;
+    return ((unsigned long long)rd() << 32) ^ (unsigned long long)rd();
+  }()};
+  constexpr unsigned long long kMask = (1ull << (64 - kArrivalBits)) - 1;
+  for (;;) {
+    const unsigned long long t = tag.fetch_add(1) & kMask;
+    if (t != 0) return t;
+  }
 }
 
 // Workspace of the stream kernel: partial slots (units + CTAs) x query
@@ -2391,7 +2514,7 @@ StreamWs stream_ws_layout(const DecodeArgs& a, const Plan& p) {
   w.acc_off = 0;
   w.ml_off = (slots * 128 * sizeof(float) + 255) & ~(size_t)255;
   w.cnt_off = (w.ml_off + slots * sizeof(float2) + 255) & ~(size_t)255;
-  w.bytes = w.cnt_off + units * sizeof(int) + 256;
+  w.bytes = w.cnt_off + units * sizeof(unsigned long long) + 256;
   return w;
 }
 
@@ -2413,16 +2536,11 @@ int launch_fast_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_
     uint8_t* base = reinterpret_cast<uint8_t*>(ws_acc);
     float* sacc = reinterpret_cast<float*>(base + w.acc_off);
     float2* sml = reinterpret_cast<float2*>(base + w.ml_off);
-    int* scnt = reinterpret_cast<int*>(base + w.cnt_off);
-    const cudaError_t me = cudaMemsetAsync(scnt, 0, w.units * sizeof(int), stream);
-    if (me != cudaSuccess) {
-      set_error(std::string("decode counter reset failed: ") + cudaGetErrorString(me));
-      return kCudaError;
-    }
+    auto* scnt = reinterpret_cast<unsigned long long*>(base + w.cnt_off);
     skern<<<p.n_ctas, kStreamThreads, SC::kSmemBytes, stream>>>(
         mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out, sacc, sml, scnt,
         a.num_seqs, a.num_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq,
-        a.sm_scale * kLog2e, device_error_word());
+        a.sm_scale * kLog2e, std::max(1, p.min_pages), next_launch_tag(), device_error_word());
     return kOk;
   }
   auto kern = decode_fast_kernel<BS, HG, G>;
@@ -2576,7 +2694,7 @@ int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
   }
   // Splits > 1 and empty sequences are finished by the combine.
   dim3 cgrid(a.num_seqs, a.num_heads);
-  decode_combine_kernel<<<cgrid, 128, 0, stream>>>(a.seq_lens, ws_acc, ws_ml, a.out, a.num_heads,
+  decode_combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(a.seq_lens, ws_acc, ws_ml, a.out, a.num_heads,
                                                    a.head_dim, a.block_size, a.max_blocks_per_seq,
                                                    p.pages_per_split, p.max_splits);
   e = cudaGetLastError();

@@ -174,7 +174,10 @@ __global__ void __launch_bounds__(kCT, 1)
     const uint32_t src = smem_u32(my_slice);
     push_to_cta(cluster_addr(src, tid), src, slice_bytes, cluster_addr(smem_u32(bar), tid));
   }
-  if (!mbar_wait_bounded(bar, 0, err)) record_error(err, kDevWaitTimeout);
+  if (!mbar_wait_bounded(bar, 0, err)) {
+    record_error(err, kDevWaitTimeout);
+    mbar_drain(bar, 0);  // no push may land after this CTA has exited
+  }
 
   // ---- 3. histogram of all keys over [min, max] ------------------------------
   if (warp == 0) {

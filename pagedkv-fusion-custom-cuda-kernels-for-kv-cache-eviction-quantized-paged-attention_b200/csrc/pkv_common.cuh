@@ -41,6 +41,43 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
 }
 
+// Arrival on a GPU-wide counter that publishes this CTA's earlier global
+// writes and acquires the other arrivals' writes: release / acquire at GPU
+// scope on the one atomic (cumulative, so writes of other threads of the CTA
+// ordered before it by a CTA barrier are covered), instead of a
+// sequentially consistent fence in every writing thread.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+// 64-bit add with release / acquire at GPU scope.
+__device__ __forceinline__ unsigned long long atomic_add_acq_rel_gpu_u64(unsigned long long* p,
+                                                                       unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;"
+               : "=l"(old)
+               : "l"(p), "l"(v)
+               : "memory");
+  return old;
+}
+
+// 64-bit compare-and-swap with release / acquire at GPU scope.
+__device__ __forceinline__ unsigned long long atomic_cas_acq_rel_gpu(unsigned long long* p,
+                                                                   unsigned long long cmp,
+                                                                   unsigned long long val) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;"
+               : "=l"(old)
+               : "l"(p), "l"(cmp), "l"(val)
+               : "memory");
+  return old;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -125,18 +162,30 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t pa
   return done != 0;
 }
 
+// Suspend-time hint of a waiting poll, in ns (0: polls without a hint).
+#ifndef PKV_MBAR_SUSPEND_NS
+#define PKV_MBAR_SUSPEND_NS 100000u
+#endif
+
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
+#if PKV_MBAR_SUSPEND_NS > 0
+  return mbar_try_wait_suspend(bar, parity, PKV_MBAR_SUSPEND_NS);
+#else
+  return mbar_try_wait(bar, parity);
+#endif
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after
 // `limit_ns` nanoseconds of wall time, or as soon as any CTA has recorded a
-// wait timeout in the error word (both checked after every suspended poll of
-// at most 100 us), and returns false; the caller records kDevWaitTimeout and
-// unwinds.
+// wait timeout in the error word (both checked after every poll), and
+// returns false; the caller records kDevWaitTimeout and unwinds.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   const int* err,
                                                   uint64_t limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (;;) {
-    if (mbar_try_wait_suspend(bar, parity, 100000u)) return true;
+    if (mbar_poll(bar, parity)) return true;
     if (global_timer_ns() - t0 > limit_ns) return false;
     if (err != nullptr && *reinterpret_cast<const volatile int*>(err) == kDevWaitTimeout)
       return false;
@@ -153,7 +202,7 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity,
                                            uint64_t limit_ns = 200000000ull) {
   if (mbar_try_wait(bar, parity)) return;
   const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait_suspend(bar, parity, 100000u))
+  while (!mbar_poll(bar, parity))
     if (global_timer_ns() - t0 > limit_ns) return;
 }
 

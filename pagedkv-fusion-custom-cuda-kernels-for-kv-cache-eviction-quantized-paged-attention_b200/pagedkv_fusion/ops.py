@@ -38,6 +38,7 @@ __all__ = [
     "EvictionPlan",
     "attention_stats",
     "quant_paged_attention",
+    "DecodePlan",
 ]
 
 
@@ -225,3 +226,47 @@ def quant_paged_attention(q, k_cache_q, k_scale, v_cache_q, v_scale, block_table
                                   st.to_device(block_tables, torch.int32),
                                   st.to_device(seq_lens, torch.int32), sm_scale)
     return st.back(out)
+
+
+class DecodePlan:
+    """``quant_paged_attention`` captured once as a CUDA graph over fixed
+    buffers, for a decode loop whose batch shape stays put: each step the
+    caller writes the new queries into ``q`` and the new tables / lengths
+    into ``block_tables`` / ``seq_lens`` (in place), appends to the caches,
+    then calls :meth:`run`.  A replay skips the argument checks, the
+    workspace allocation and the host-side launch work of the eager call;
+    the output lands in the same ``out`` tensor every time.
+
+    All inputs must be contiguous CUDA tensors that keep their storage while
+    the plan is used (``seq_lens`` int32).  The kernel choice is made for
+    the capture's shapes; lengths up to ``block_tables``' width are
+    handled by the same graph.
+    """
+
+    def __init__(self, q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables, seq_lens,
+                 sm_scale: float):
+        C = _lib()
+        bufs = (q, k_cache_q, k_scale, v_cache_q, v_scale, block_tables, seq_lens)
+        if not _all_cuda(*bufs):
+            raise RuntimeError("DecodePlan needs CUDA tensors (it binds their storage)")
+        if not all(t.is_contiguous() for t in bufs):
+            raise RuntimeError("DecodePlan needs contiguous tensors (a copy would not be rebound)")
+        if q.dtype != torch.float32 or block_tables.dtype != torch.int32 or \
+                seq_lens.dtype != torch.int32:
+            raise RuntimeError("DecodePlan needs float32 q and int32 block_tables / seq_lens")
+        self._inputs = bufs
+        args = bufs + (float(sm_scale),)
+        dev = q.device
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            C.quant_paged_attention(*args)  # kernel attributes, tensor maps
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph):
+            self.out = C.quant_paged_attention(*args)
+
+    def run(self):
+        """Replays the capture on the current stream; returns ``out``."""
+        self._graph.replay()
+        return self.out

@@ -453,6 +453,40 @@ def test_attention_deterministic(cuda):
     assert torch.equal(run_attention(args), run_attention(args))
 
 
+@pytest.mark.parametrize("shape", [(8, 512, 8), (37, 1000, 8), (3, 5000, 4)])
+def test_stream_workspace_needs_no_initialisation(cuda, shape):
+    """The stream kernel's arrival counters carry a per-launch tag: a
+    workspace holding random bytes, or the counters a previous launch left,
+    gives the same output, bit for bit, as a fresh one."""
+    S, L, hkv = shape
+    r = np.random.default_rng(S)
+    q, k, v, bt, sl, sm = problems.make_paged_kv_problem(r, S, hkv, hkv, 128, 16, L)
+    args = [dev(a) if isinstance(a, np.ndarray) else a for a in quantized_problem(q, k, v, bt, sl, sm)]
+    qd, kq, ks, vq, vs, btd, sld, smf = args
+    assert cuda.quant_paged_attention_kernel_launches(S, hkv, hkv, 128, 16, bt.shape[1]) == 1
+    nbytes = cuda._attn_ws(S, hkv, hkv, 128, 16, bt.shape[1])
+    cuda.read_device_error(reset=True)
+    want = cuda.quant_paged_attention(*args)
+
+    def call(ws):
+        out = torch.empty_like(qd)
+        rc = cuda._attn(qd.data_ptr(), kq.data_ptr(), ks.data_ptr(), vq.data_ptr(), vs.data_ptr(),
+                        btd.data_ptr(), sld.data_ptr(), out.data_ptr(), S, hkv, hkv, 128, 16,
+                        kq.shape[0], bt.shape[1], float(smf), ws.data_ptr(), ws.numel(),
+                        torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        return out
+
+    garbage = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda")
+    assert torch.equal(call(garbage), want)
+    ones = torch.full((nbytes,), 0xFF, dtype=torch.uint8, device="cuda")
+    assert torch.equal(call(ones), want)
+    reused = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    for _ in range(3):  # counters left by the previous launch
+        assert torch.equal(call(reused), want)
+    assert cuda.read_device_error(reset=True) == 0
+
+
 def test_attention_bad_block_id_is_reported(cuda):
     q, k, v, bt, sl, sm = problems.make_paged_kv_problem(np.random.default_rng(8), 2, 8, 8, 128,
                                                          16, 64)
