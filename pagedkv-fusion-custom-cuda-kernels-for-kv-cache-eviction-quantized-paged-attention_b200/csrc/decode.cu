@@ -600,11 +600,12 @@ __global__ void __launch_bounds__(kFastThreads, 2)
 //
 // A table warp fills a double-buffered chunk table (block-table entries,
 // scales, token count and, for a new unit, the query rows by bulk copy) and
-// publishes each half with an mbarrier (meta_full).  It fetches the first
-// two chunks together before any page load is issued, so these small loads
-// do not queue behind the GPU-wide burst of page loads, and later chunks
-// one chunk ahead.  The TMA warp then only waits for a chunk's table before
-// issuing its K and V pages back to back.  The per-head maximum of a
+// publishes each half in two steps: the block ids (phys_full), then the rest
+// (meta_full).  It fetches the first two chunks together before any page
+// load is issued, so these small loads do not queue behind the GPU-wide
+// burst of page loads, and later chunks one chunk ahead.  The TMA warp only
+// waits for a chunk's block ids before issuing its K and V pages back to
+// back, so the scale loads overlap the first page loads.  The per-head maximum of a
 // chunk's logits is gathered while the K pages are read, so the softmax is
 // a single vectorised pass.
 //
@@ -651,7 +652,7 @@ struct StreamCfg {
   static constexpr int kOffRed = (kOffPseq + (kStreamMaxSeqs + 1) * 4 + 15) & ~15;
   static constexpr int kRedBytes = F::kVR > 1 ? kConsumerWarps * F::kGPW * 128 * 4 : 0;
   static constexpr int kOffBar = (kOffRed + kRedBytes + 15) & ~15;
-  static constexpr int kSmemBytes = kOffBar + (2 * kFastStages + 4) * 8 + 1024;
+  static constexpr int kSmemBytes = kOffBar + (2 * kFastStages + 6) * 8 + 1024;
   // two CTAs per SM (228 KB of shared memory, 1 KB reserved per CTA)
   static_assert(2 * (kSmemBytes + 1024) <= 228 * 1024, "stream kernel shared memory");
   static_assert(F::kMaxPages <= 32, "one chunk page per table-warp lane");
@@ -666,15 +667,21 @@ struct StreamChunk {
   bool seg_first, seg_last, whole;
 };
 
-// Walks one CTA's flattened page range [pos, end) in chunks of at most
-// max_pages pages; every thread of the CTA runs its own copy identically.
+// Walks one CTA's share [pos, end) of the flattened range in chunks of at
+// most max_pages pages; every thread of the CTA runs its own copy
+// identically.  The range is virtual: a unit of n pages spans alpha + n
+// positions, the first alpha standing for the fixed cost of one more chunk
+// (its table, the K -> softmax -> V hand-offs, its partial and merge), so a
+// CTA whose share starts a unit takes about alpha fewer pages.  pseq[s] is
+// the virtual per-group prefix: sequence s spans ng * (alpha + pages) virtual
+// positions, 0 when it has no page.  Chunk fields are in real pages.
 struct StreamIter {
   long long pos, end, cta_start;
-  int s, g, S, ng, max_pages;
+  int s, g, S, ng, max_pages, alpha;
   const int* pseq;
 
   __device__ void init(long long start, long long stop, const int* ps, int num_seqs, int groups,
-                       int mp) {
+                       int mp, int a) {
     pos = start;
     end = stop;
     cta_start = start;
@@ -682,6 +689,7 @@ struct StreamIter {
     S = num_seqs;
     ng = groups;
     max_pages = mp;
+    alpha = a;
     s = 0;
     g = 0;
     if (pos >= end) return;
@@ -691,37 +699,50 @@ struct StreamIter {
       if ((long long)pseq[mid] * ng <= pos) lo = mid; else hi = mid - 1;
     }
     s = lo;
-    const int pages = pseq[s + 1] - pseq[s];
-    g = (int)((pos - (long long)pseq[s] * ng) / pages);
+    const int vp = pseq[s + 1] - pseq[s];
+    g = (int)((pos - (long long)pseq[s] * ng) / vp);
   }
 
   __device__ bool next(StreamChunk& c) {
-    if (pos >= end) return false;
-    const int pages = pseq[s + 1] - pseq[s];
-    const long long ustart = (long long)pseq[s] * ng + (long long)g * pages;
-    const int lp0 = (int)(pos - ustart);
-    const long long seg_lo_abs = cta_start > ustart ? cta_start : ustart;
-    const int seg_lo = (int)(seg_lo_abs - ustart);
-    const long long uend = ustart + pages;
-    const int seg_hi = (int)((end < uend ? end : uend) - ustart);
-    const int np = min(max_pages, seg_hi - lp0);
-    c.s = s;
-    c.g = g;
-    c.lp0 = lp0;
-    c.np = np;
-    c.seg_first = lp0 == seg_lo;
-    c.seg_last = lp0 + np == seg_hi;
-    c.whole = seg_lo == 0 && seg_hi == pages;
-    pos += np;
-    if (c.seg_last && pos < end) {
-      if (++g == ng) {
-        g = 0;
-        do {
-          ++s;
-        } while (s < S - 1 && pseq[s + 1] == pseq[s]);
+    while (pos < end) {
+      const int vp = pseq[s + 1] - pseq[s];
+      const long long ustart = (long long)pseq[s] * ng + (long long)g * vp;
+      const long long first_page = ustart + alpha;  // virtual position of real page 0
+      const long long uend = ustart + vp;
+      const long long seg_hi_v = end < uend ? end : uend;
+      if (pos < first_page) pos = first_page;  // the unit's overhead positions
+      if (pos < seg_hi_v) {
+        const long long seg_lo_v = cta_start > first_page ? cta_start : first_page;
+        const int pages = vp - alpha;
+        const int lp0 = (int)(pos - first_page);
+        const int seg_lo = (int)(seg_lo_v - first_page);
+        const int seg_hi = (int)(seg_hi_v - first_page);
+        const int np = min(max_pages, seg_hi - lp0);
+        c.s = s;
+        c.g = g;
+        c.lp0 = lp0;
+        c.np = np;
+        c.seg_first = lp0 == seg_lo;
+        c.seg_last = lp0 + np == seg_hi;
+        c.whole = seg_lo == 0 && seg_hi == pages;
+        pos += np;
+        if (c.seg_last && pos < end) advance();
+        return true;
       }
+      // nothing real of this unit in the share: on to the next unit
+      pos = seg_hi_v;
+      if (pos < end) advance();
     }
-    return true;
+    return false;
+  }
+
+  __device__ void advance() {  // the next unit with pages
+    if (++g == ng) {
+      g = 0;
+      do {
+        ++s;
+      } while (s < S - 1 && pseq[s + 1] == pseq[s]);
+    }
   }
 };
 
@@ -740,8 +761,67 @@ constexpr uint32_t kNegInfKey = 0x007fffffu;  // float_max_key(-inf)
 __device__ __forceinline__ int page_owner(long long x, long long P, int C) {
   return (int)(((x + 1) * C - 1) / P);
 }
-__device__ __forceinline__ bool cta_owns_pages(long long P, int c, int C) {
-  return P * c / C < P * (c + 1) / C;
+
+// First and last CTA owning pages of unit (s, g) in the virtual layout of
+// StreamIter.
+__device__ __forceinline__ void unit_owners(const int* pseq, int s, int g, int ng, int alpha,
+                                            long long P, int n_ctas, int& first, int& last) {
+  const int vp = pseq[s + 1] - pseq[s];
+  const long long page0 = (long long)pseq[s] * ng + (long long)g * vp + alpha;
+  first = page_owner(page0, P, n_ctas);
+  last = page_owner(page0 + (vp - alpha) - 1, P, n_ctas);
+}
+
+// A unit split across more than kMergeGroup CTAs merges in two levels: the
+// last arrival of each group of kMergeGroup consecutive CTAs merges the
+// group's partials into the group's first slot, and the last group merges
+// those.
+constexpr int kMergeGroup = 16;
+
+// Merges n partial rows (acc relative to exp2(m), with (m, l)) of one query
+// head, row j at slot slot_of(j): a = sum_j w_j acc_j and den = sum_j w_j l_j
+// with w_j = exp2(m_j - M), M = max_j m_j; rows with m = -inf add nothing.
+// Rows are added in index order (deterministic), kMergeDepth in flight.
+template <typename SlotFn>
+__device__ __forceinline__ void merge_partials(const float* __restrict__ ws_acc,
+                                               const float2* __restrict__ ws_ml, int n, int lane,
+                                               float4& a, float& M, float& den, SlotFn slot_of) {
+  auto load_ml = [&](int j) {
+    return j < n ? __ldcg(&ws_ml[slot_of(j)]) : make_float2(-INFINITY, 0.0f);
+  };
+  const float2 ml0 = load_ml(lane);  // the first 32 are kept for the second pass
+  M = ml0.x;
+  for (int b = 32; b < n; b += 32) M = fmaxf(M, load_ml(b + lane).x);
+  M = warp_max(M);
+  den = 0.0f;
+  a = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int b = 0; b < n; b += 32) {
+    const float2 ml = b == 0 ? ml0 : load_ml(b + lane);
+    float w = 0.0f;
+    if (ml.x != -INFINITY) {
+      w = exp2f(ml.x - M);
+      den += w * ml.y;
+    }
+    const int nb = min(32, n - b);
+    for (int j0 = 0; j0 < nb; j0 += kMergeDepth) {
+      float4 x[kMergeDepth];
+#pragma unroll
+      for (int jj = 0; jj < kMergeDepth; ++jj)
+        x[jj] = __ldcg(reinterpret_cast<const float4*>(ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * 128) +
+                       lane);
+#pragma unroll
+      for (int jj = 0; jj < kMergeDepth; ++jj) {
+        const float wj = __shfl_sync(0xffffffffu, w, (j0 + jj) & 31);
+        if (j0 + jj < nb && wj != 0.0f) {
+          a.x += wj * x[jj].x;
+          a.y += wj * x[jj].y;
+          a.z += wj * x[jj].z;
+          a.w += wj * x[jj].w;
+        }
+      }
+    }
+  }
+  den = warp_sum(den);
 }
 
 // Arrival counters need no reset before a launch.  A counter holds
@@ -784,8 +864,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
                          float* __restrict__ ws_acc, float2* __restrict__ ws_ml,
                          unsigned long long* __restrict__ unit_arrivals, int num_seqs, int num_heads,
                          int num_kv_heads, int64_t num_blocks, int max_blocks_per_seq,
-                         float qk_scale, int min_pages, unsigned long long launch_tag,
-                         int* err) {
+                         float qk_scale, int min_pages, int unit_cost,
+                         unsigned long long launch_tag, int* err) {
   using F = FastCfg<BS, HG, G>;
   using C = StreamCfg<BS, HG, G>;
   extern __shared__ uint8_t smem_raw[];
@@ -802,6 +882,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
   uint64_t* empty = full + kFastStages;
   uint64_t* meta_full = empty + kFastStages;  // [2]: chunk table half published
   uint64_t* chunk_free = meta_full + 2;       // [2]: chunk table half released
+  uint64_t* phys_full = chunk_free + 2;       // [2]: the half's block ids published
   const uint32_t stage_base = smem_u32(smem);
 
   const int tid = threadIdx.x;
@@ -811,7 +892,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
   const int ng = num_kv_heads / HG;
   const int grid_ctas = gridDim.x;
 
-  // ---- pages per sequence and their prefix (every CTA, identically) -------
+  // ---- virtual pages per sequence (unit_cost + pages, per KV-head group;
+  // 0 without pages) and their prefix (every CTA, identically) -------------
   constexpr int kPer = (kStreamMaxSeqs + kStreamThreads - 1) / kStreamThreads;
   int mine[kPer];
   int sum = 0;
@@ -821,8 +903,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
     mine[i] = 0;
     if (s < S) {
       const int L = seq_lens[s];
-      mine[i] = covered_pages(L, BS, max_blocks_per_seq);
-      if (blockIdx.x == 0 && L > mine[i] * BS) record_error(err, kDevSeqTooLong);
+      const int pages = covered_pages(L, BS, max_blocks_per_seq);
+      if (blockIdx.x == 0 && L > pages * BS) record_error(err, kDevSeqTooLong);
+      mine[i] = pages > 0 ? pages + unit_cost : 0;
     }
     sum += mine[i];
   }
@@ -841,6 +924,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&meta_full[i], 1);
       mbar_init(&chunk_free[i], 2);  // consumers (softmax done) + TMA warp (pages issued)
+      mbar_init(&phys_full[i], 1);
     }
     mbar_fence_init();
   }
@@ -872,7 +956,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
   if (c_begin >= c_end) return;  // uniform
 
   StreamIter it;
-  it.init(c_begin, c_end, s_pseq, S, ng, F::kMaxPages);
+  it.init(c_begin, c_end, s_pseq, S, ng, F::kMaxPages, unit_cost);
   StreamChunk ch;
 
   // ---- table warp: chunk tables one chunk ahead ---------------------------
@@ -896,12 +980,21 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
         vs[jj] = phys >= 0 ? v_scale[si + jj] : 0.0f;
       }
     };
-    // Writes chunk c's table into half b and publishes it on meta_full[b].
-    auto publish = [&](int b, const StreamChunk& c, bool new_unit, int phys,
+    // Writes chunk c's block ids into half b and publishes them on
+    // phys_full[b]: the TMA warp issues the pages while the scales load.
+    auto publish_phys = [&](int b, const StreamChunk& c, int phys) {
+      uint8_t* meta = smem + C::kOffMeta + b * C::kMetaBytes;
+      if (lane < c.np) reinterpret_cast<int*>(meta + C::kMetaPhys)[lane] = phys;
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&phys_full[b]);
+    };
+    // Writes the rest of chunk c's table into half b and publishes it on
+    // meta_full[b].
+    auto publish = [&](int b, const StreamChunk& c, bool new_unit,
                        const float (&ks)[HG], const float (&vs)[HG]) {
       uint8_t* meta = smem + C::kOffMeta + b * C::kMetaBytes;
       if (lane < c.np) {
-        reinterpret_cast<int*>(meta + C::kMetaPhys)[lane] = phys;
 #pragma unroll
         for (int jj = 0; jj < HG; ++jj) {
           reinterpret_cast<float*>(meta + C::kMetaKs)[lane * HG + jj] = ks[jj];
@@ -914,7 +1007,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
         if (lane == 0) reinterpret_cast<float*>(meta + C::kMetaVmax)[jj] = v;
       }
       if (lane == 0) {
-        const int pages = s_pseq[c.s + 1] - s_pseq[c.s];
+        const int pages = s_pseq[c.s + 1] - s_pseq[c.s] - unit_cost;
         const int Ls = min(max(seq_lens[c.s], 0), pages * BS);
         *reinterpret_cast<int*>(meta + C::kMetaT) = min(Ls, (c.lp0 + c.np) * BS) - c.lp0 * BS;
       }
@@ -944,10 +1037,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       float ks0[HG], vs0[HG], ks1[HG], vs1[HG];
       const int p0 = load_phys(c0);
       const int p1 = have1 ? load_phys(c1) : -1;
+      publish_phys(0, c0, p0);
+      if (have1) publish_phys(1, c1, p1);
       load_scales(c0, p0, ks0, vs0);
       if (have1) load_scales(c1, p1, ks1, vs1);
-      publish(0, c0, true, p0, ks0, vs0);
-      if (have1) publish(1, c1, c1.s != c0.s || c1.g != c0.g, p1, ks1, vs1);
+      publish(0, c0, true, ks0, vs0);
+      if (have1) publish(1, c1, c1.s != c0.s || c1.g != c0.g, ks1, vs1);
     }
     int published = have1 ? 2 : 1;
     if (have1) {
@@ -962,8 +1057,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         float ks[HG], vs[HG];
         const int ph = load_phys(cur);
+        publish_phys(b, cur, ph);
         load_scales(cur, ph, ks, vs);
-        publish(b, cur, cur.s != prev.s || cur.g != prev.g, ph, ks, vs);
+        publish(b, cur, cur.s != prev.s || cur.g != prev.g, ks, vs);
         prev = cur;
       }
     }
@@ -981,13 +1077,21 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
          // whose first page is here
         StreamIter w = it;
         StreamChunk c;
-        while (w.next(c))
-          if (c.lp0 == 0 && !c.whole) stamp_unit(&unit_arrivals[c.s * ng + c.g], launch_tag);
+        const int me = blockIdx.x;
+        while (w.next(c)) {
+          if (!c.seg_first || c.whole) continue;
+          int first, last;
+          unit_owners(s_pseq, c.s, c.g, ng, unit_cost, P, n_ctas, first, last);
+          const int u = c.s * ng + c.g;
+          if (me == first) stamp_unit(&unit_arrivals[u], launch_tag);
+          if (last - first + 1 > kMergeGroup && (me - first) % kMergeGroup == 0)
+            stamp_unit(&unit_arrivals[S * ng + u + me], launch_tag);  // its group's counter
+        }
       }
       int ns = 0;
       for (int i = 0; it.next(ch); ++i) {
         const int b = i & 1;
-        if (!mbar_wait_bounded(&meta_full[b], (uint32_t)(i >> 1) & 1u, err)) {
+        if (!mbar_wait_bounded(&phys_full[b], (uint32_t)(i >> 1) & 1u, err)) {
           record_error(err, kDevWaitTimeout);
           break;
         }
@@ -1307,75 +1411,67 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
             if (lane == 0) ws_ml[slot] = s_run[hg];
           }
         }
-        // the unit's CTAs, in page order
-        const int pages = s_pseq[ch.s + 1] - s_pseq[ch.s];
-        const long long ustart = (long long)s_pseq[ch.s] * ng + (long long)ch.g * pages;
-        const int first = page_owner(ustart, P, n_ctas);
-        const int last = page_owner(ustart + pages - 1, P, n_ctas);
-        const bool all_own = P >= n_ctas;  // then every CTA owns >= 1 page
+        // the unit's CTAs [first, last] in page order: every one owns pages
+        // (n_ctas <= P gives each CTA at least one position)
+        int first, last;
+        unit_owners(s_pseq, ch.s, ch.g, ng, unit_cost, P, n_ctas, first, last);
+        const int nseg = last - first + 1;
+        const int ngroups = (nseg + kMergeGroup - 1) / kMergeGroup;
+        const int g_lo = first + (int)(blockIdx.x - first) / kMergeGroup * kMergeGroup;
+        const int g_hi = min(last, g_lo + kMergeGroup - 1);
+        const int n_units = S * ng;
         // every partial store of this CTA is ordered before thread 0's
         // release by the barrier; the last arrival acquires all of them
         named_barrier(1, kConsumers);
         if (tid == 0) {
-          // with fewer pages than CTAs every CTA owns at most one page, so
-          // the unit's pages have distinct owners; otherwise every CTA in
-          // [first, last] owns some
-          const int nseg = all_own ? last - first + 1 : pages;
-          const int r = arrive_on_unit(&unit_arrivals[u], launch_tag, nseg);
+          const int r = ngroups == 1
+                            ? arrive_on_unit(&unit_arrivals[u], launch_tag, nseg)
+                            : arrive_on_unit(&unit_arrivals[n_units + u + g_lo], launch_tag,
+                                             g_hi - g_lo + 1);
           if (r < 0) record_error(err, kDevWaitTimeout);
           s_tmp[32] = r == 1;
         }
         named_barrier(1, kConsumers);
-        if (s_tmp[32] && v_r == 0) {  // this CTA completed the set: merge
+        // this CTA completed its group: merge it; with more than one group the
+        // group's partial goes to its first slot and the last group to
+        // complete merges the groups' partials (a second pass)
+        int m_lo = g_lo, m_n = g_hi - g_lo + 1, m_stride = 1;
+        bool final_pass = ngroups == 1;
+        bool merging = s_tmp[32] != 0;
+        while (merging) {
+          if (v_r == 0) {
 #pragma unroll 1
-          for (int g = 0; g < F::kGPW; ++g) {
-            const int hg = v_jj * G + g0 + g;
-            auto slot_of = [&](int c) { return ((int64_t)u + c) * F::kNHG + hg; };
-            // (m, l) of this lane's CTA; the first 32 are kept for the second pass
-            auto load_ml = [&](int c) {
-              return c <= last && (all_own || cta_owns_pages(P, c, n_ctas))
-                         ? __ldcg(&ws_ml[slot_of(c)])
-                         : make_float2(-INFINITY, 0.0f);
-            };
-            const float2 ml0 = load_ml(first + lane);
-            float M = ml0.x;
-            for (int b = first + 32; b <= last; b += 32) M = fmaxf(M, load_ml(b + lane).x);
-            M = warp_max(M);
-            float den = 0.0f;
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int b = first; b <= last; b += 32) {
-              const float2 ml = b == first ? ml0 : load_ml(b + lane);
-              float w = 0.0f;
-              if (ml.x != -INFINITY) {
-                w = exp2f(ml.x - M);
-                den += w * ml.y;
-              }
-              const int nb = min(32, last - b + 1);
-              // kMergeDepth partial rows in flight at a time; rows of CTAs that
-              // own no page of the unit (weight 0) are read but not added
-              for (int j0 = 0; j0 < nb; j0 += kMergeDepth) {
-                float4 x[kMergeDepth];
-#pragma unroll
-                for (int jj = 0; jj < kMergeDepth; ++jj)
-                  x[jj] = __ldcg(reinterpret_cast<const float4*>(
-                                     ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * 128) + lane);
-#pragma unroll
-                for (int jj = 0; jj < kMergeDepth; ++jj) {
-                  const float wj = __shfl_sync(0xffffffffu, w, (j0 + jj) & 31);
-                  if (j0 + jj < nb && wj != 0.0f) {
-                    a.x += wj * x[jj].x;
-                    a.y += wj * x[jj].y;
-                    a.z += wj * x[jj].z;
-                    a.w += wj * x[jj].w;
-                  }
-                }
+            for (int g = 0; g < F::kGPW; ++g) {
+              const int hg = v_jj * G + g0 + g;
+              float4 a;
+              float M, den;
+              merge_partials(ws_acc, ws_ml, m_n, lane, a, M, den, [&](int j) {
+                return ((int64_t)u + m_lo + j * m_stride) * F::kNHG + hg;
+              });
+              if (final_pass) {
+                const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+                reinterpret_cast<float4*>(out + ((int64_t)ch.s * num_heads + (int64_t)j0 * G + hg) * 128)[lane] =
+                    make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+              } else {
+                const int64_t slot = ((int64_t)u + g_lo) * F::kNHG + hg;
+                reinterpret_cast<float4*>(ws_acc + slot * 128)[lane] = a;
+                if (lane == 0) ws_ml[slot] = make_float2(M, den);
               }
             }
-            den = warp_sum(den);
-            const float inv = den > 0.0f ? 1.0f / den : 0.0f;
-            reinterpret_cast<float4*>(out + ((int64_t)ch.s * num_heads + (int64_t)j0 * G + hg) * 128)[lane] =
-                make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
           }
+          if (final_pass) break;
+          named_barrier(1, kConsumers);  // the group's partial is stored
+          if (tid == 0) {
+            const int r = arrive_on_unit(&unit_arrivals[u], launch_tag, ngroups);
+            if (r < 0) record_error(err, kDevWaitTimeout);
+            s_tmp[33] = r == 1;
+          }
+          named_barrier(1, kConsumers);
+          merging = s_tmp[33] != 0;
+          m_lo = first;
+          m_n = ngroups;
+          m_stride = kMergeGroup;
+          final_pass = true;
         }
       }
 #pragma unroll
@@ -2399,6 +2495,7 @@ struct Plan {
   int max_splits = 1;
   int n_ctas = 0;     // stream kernel grid
   int min_pages = 1;  // stream kernel: fewest pages a CTA takes
+  int unit_cost = 0;  // stream kernel: a unit's fixed cost, in pages
 };
 
 int sm_count() {
@@ -2481,6 +2578,7 @@ Plan make_plan(const DecodeArgs& a) {
     const int forced = env_int("PKV_DECODE_CTAS", 0);
     p.n_ctas = forced > 0 ? forced : 2 * sm_count();
     p.min_pages = std::max(1, env_int("PKV_STREAM_MIN_PAGES", 4));
+    p.unit_cost = std::max(0, env_int("PKV_STREAM_UNIT_COST", 4));
   }
   return p;
 }
@@ -2514,7 +2612,8 @@ StreamWs stream_ws_layout(const DecodeArgs& a, const Plan& p) {
   w.acc_off = 0;
   w.ml_off = (slots * 128 * sizeof(float) + 255) & ~(size_t)255;
   w.cnt_off = (w.ml_off + slots * sizeof(float2) + 255) & ~(size_t)255;
-  w.bytes = w.cnt_off + units * sizeof(unsigned long long) + 256;
+  // arrival counters: one per unit, then one per (unit + CTA) for two-level merges
+  w.bytes = w.cnt_off + (2 * units + p.n_ctas) * sizeof(unsigned long long) + 256;
   return w;
 }
 
@@ -2540,7 +2639,8 @@ int launch_fast_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_
     skern<<<p.n_ctas, kStreamThreads, SC::kSmemBytes, stream>>>(
         mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out, sacc, sml, scnt,
         a.num_seqs, a.num_heads, a.num_kv_heads, a.num_blocks, a.max_blocks_per_seq,
-        a.sm_scale * kLog2e, std::max(1, p.min_pages), next_launch_tag(), device_error_word());
+        a.sm_scale * kLog2e, std::max(1, p.min_pages), std::max(0, p.unit_cost), next_launch_tag(),
+        device_error_word());
     return kOk;
   }
   auto kern = decode_fast_kernel<BS, HG, G>;

@@ -453,6 +453,51 @@ def test_attention_deterministic(cuda):
     assert torch.equal(run_attention(args), run_attention(args))
 
 
+@pytest.mark.parametrize("unit_cost,min_pages", [(0, 1), (0, 4), (3, 4), (7, 1), (2, 16), (40, 2)])
+@pytest.mark.parametrize("shape", [(37, 1000, 8), (2, 9000, 8), (5, 300, 2)])
+def test_stream_share_parameters_match_oracle(cuda, monkeypatch, unit_cost, min_pages, shape):
+    """The stream kernel's page shares (a unit's fixed cost counted in pages,
+    the fewest pages per CTA) move the CTA boundaries and so the partials
+    and merges; every setting stays within the attention tolerance, on
+    ragged lengths with empty sequences."""
+    S, L, hkv = shape
+    r = np.random.default_rng(S * 131 + L)
+    q, k, v, bt, sl, sm = problems.make_paged_kv_problem(r, S, hkv, hkv, 128, 16, L)
+    sl[::4] = 0                      # sequences without pages
+    sl[1::5] = np.minimum(sl[1::5], 16)  # one page or less
+    args = quantized_problem(q, k, v, bt, sl, sm)
+    want = c_oracle.paged_attention(*args)
+    monkeypatch.setenv("PKV_STREAM_UNIT_COST", str(unit_cost))
+    monkeypatch.setenv("PKV_STREAM_MIN_PAGES", str(min_pages))
+    assert cuda.quant_paged_attention_kernel_launches(S, hkv, hkv, 128, 16, bt.shape[1]) == 1
+    cuda.read_device_error(reset=True)
+    got = run_attention(args)
+    assert_attention_close(got, want)
+    assert torch.equal(got, run_attention(args))  # deterministic for a fixed setting
+    assert cuda.read_device_error(reset=True) == 0
+
+
+@pytest.mark.parametrize("ctas", [0, 16, 17, 33, 200])
+def test_stream_long_sequence_two_level_merge(cuda, monkeypatch, ctas):
+    """One long sequence (778 pages) over many CTAs: more than 16 partials
+    per unit merge in two levels (groups of 16, then the groups); grids of
+    17 / 33 CTAs leave a group of one.  0 = the default grid."""
+    r = np.random.default_rng(321)
+    q, k, v, bt, sl, sm = problems.make_paged_kv_problem(r, 1, 8, 8, 128, 16, 32768)
+    sl[:] = bt.shape[1] * 16 - 5  # the table's every page, the last one partial
+    assert bt.shape[1] > 16 * 16  # enough pages for every grid tried here
+    args = quantized_problem(q, k, v, bt, sl, sm)
+    want = c_oracle.paged_attention(*args)
+    if ctas:
+        monkeypatch.setenv("PKV_DECODE_CTAS", str(ctas))
+    monkeypatch.setenv("PKV_STREAM_MIN_PAGES", "1")
+    cuda.read_device_error(reset=True)
+    got = run_attention(args)
+    assert_attention_close(got, want)
+    assert torch.equal(got, run_attention(args))
+    assert cuda.read_device_error(reset=True) == 0
+
+
 @pytest.mark.parametrize("shape", [(8, 512, 8), (37, 1000, 8), (3, 5000, 4)])
 def test_stream_workspace_needs_no_initialisation(cuda, shape):
     """The stream kernel's arrival counters carry a per-launch tag: a
