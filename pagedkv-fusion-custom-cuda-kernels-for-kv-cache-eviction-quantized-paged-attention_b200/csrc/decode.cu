@@ -1587,90 +1587,77 @@ __global__ void __launch_bounds__(kGenThreads)
 // Combine
 // ===========================================================================
 
-constexpr int kCombineThreads = 128;
-constexpr int kCombineChunk = 1024;  // split weights staged in shared memory at a time
+constexpr int kCombineThreads = 128;  // four (sequence, query head) pairs per CTA
+constexpr int kCombineDepth = 8;      // partial rows in flight per lane
 
-__device__ __forceinline__ float block_max_128(float v, float* red) {
-  v = warp_max(v);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-}
-__device__ __forceinline__ float block_sum_128(float v, float* red) {
-  v = warp_sum(v);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  return (red[0] + red[1]) + (red[2] + red[3]);
-}
-
-// One CTA per (sequence, query head).  Latency-bound: the splits' (m, l)
-// are read by all threads at once, and each output channel keeps eight
-// partial rows in flight; accumulation runs in split order.
+// One warp per (sequence, query head): the splits' (m, l) are read one per
+// lane, M and the denominator reduced by shuffles, and each lane keeps V =
+// head_dim / 32 channels (d = lane + 32 c, coalesced) with kCombineDepth
+// partial rows in flight; rows are added in split order (deterministic).
+template <int V>
 __global__ void __launch_bounds__(kCombineThreads)
     decode_combine_kernel(const int32_t* __restrict__ seq_lens, const float* __restrict__ ws_acc,
-                          const float2* __restrict__ ws_ml, float* __restrict__ out,
-                          int num_heads, int head_dim, int bs, int max_blocks_per_seq,
-                          int pages_per_split, int max_splits) {
-  __shared__ float s_w[kCombineChunk];
-  __shared__ float s_red[kCombineThreads / 32];
-  const int seq = blockIdx.x;
-  const int h = blockIdx.y;
-  const int tid = threadIdx.x;
+                          const float2* __restrict__ ws_ml, float* __restrict__ out, int num_seqs,
+                          int num_heads, int bs, int max_blocks_per_seq, int pages_per_split,
+                          int max_splits) {
+  constexpr int D = 32 * V;
+  const int lane = threadIdx.x & 31;
+  const int64_t pair = (int64_t)blockIdx.x * (kCombineThreads / 32) + (threadIdx.x >> 5);
+  if (pair >= (int64_t)num_seqs * num_heads) return;  // whole warps
+  const int seq = (int)(pair / num_heads);
+  const int h = (int)(pair - (int64_t)seq * num_heads);
   const int n_pages = covered_pages(seq_lens[seq], bs, max_blocks_per_seq);
-  const int n_splits = (n_pages + pages_per_split - 1) / pages_per_split;
-  float* o = out + ((int64_t)seq * num_heads + h) * head_dim;
-  if (n_splits == 0) {
-    for (int d = tid; d < head_dim; d += kCombineThreads) o[d] = 0.0f;
+  const int n = (n_pages + pages_per_split - 1) / pages_per_split;
+  float* o = out + ((int64_t)seq * num_heads + h) * D;
+  if (n == 0) {
+#pragma unroll
+    for (int c = 0; c < V; ++c) o[lane + 32 * c] = 0.0f;
     return;
   }
-  if (n_splits == 1) return;  // written by the split kernel
+  if (n == 1) return;  // written by the split kernel
   const int64_t base = (int64_t)seq * max_splits * num_heads + h;
-  float M = -INFINITY;
-  for (int s = tid; s < n_splits; s += kCombineThreads)
-    M = fmaxf(M, __ldcg(&ws_ml[base + (int64_t)s * num_heads]).x);
-  M = block_max_128(M, s_red);
-  const int64_t stride = (int64_t)num_heads * head_dim;  // between splits of one head
+  auto slot_of = [&](int s) { return base + (int64_t)s * num_heads; };
+  auto load_ml = [&](int s) {
+    return s < n ? __ldcg(&ws_ml[slot_of(s)]) : make_float2(-INFINITY, 0.0f);
+  };
+  const float2 ml0 = load_ml(lane);
+  float M = ml0.x;
+  for (int b = 32; b < n; b += 32) M = fmaxf(M, load_ml(b + lane).x);
+  M = warp_max(M);
   float den = 0.0f;
-  float acc[2] = {0.0f, 0.0f};  // channels tid and tid + 128 (head_dim <= 256)
-  for (int c0 = 0; c0 < n_splits; c0 += kCombineChunk) {
-    const int cnt = min(kCombineChunk, n_splits - c0);
-    __syncthreads();  // the previous chunk's weights are consumed
-    for (int s = tid; s < cnt; s += kCombineThreads) {
-      const float2 ml = __ldcg(&ws_ml[base + (int64_t)(c0 + s) * num_heads]);
-      const float w = ml.x != -INFINITY ? exp2f(ml.x - M) : 0.0f;
-      s_w[s] = w;
+  float acc[V];
+#pragma unroll
+  for (int c = 0; c < V; ++c) acc[c] = 0.0f;
+  for (int b = 0; b < n; b += 32) {
+    const float2 ml = b == 0 ? ml0 : load_ml(b + lane);
+    float w = 0.0f;
+    if (ml.x != -INFINITY) {
+      w = exp2f(ml.x - M);
       den += w * ml.y;
     }
-    __syncthreads();
+    const int nb = min(32, n - b);
+    for (int j0 = 0; j0 < nb; j0 += kCombineDepth) {
+      float x[kCombineDepth][V];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int d = tid + r * kCombineThreads;
-      if (d < head_dim) {
-        const float* col = ws_acc + (base + (int64_t)c0 * num_heads) * head_dim + d;
-        float a = acc[r];
-        for (int s0 = 0; s0 < cnt; s0 += 8) {
-          float x[8];
+      for (int jj = 0; jj < kCombineDepth; ++jj) {
+        const float* row = ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * D + lane;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) x[j] = __ldcg(col + (int64_t)min(s0 + j, cnt - 1) * stride);
+        for (int c = 0; c < V; ++c) x[jj][c] = __ldcg(row + 32 * c);
+      }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float w = s0 + j < cnt ? s_w[s0 + j] : 0.0f;
-            if (w != 0.0f) a += w * x[j];  // rows of empty splits are not added
-          }
+      for (int jj = 0; jj < kCombineDepth; ++jj) {
+        const float wj = __shfl_sync(0xffffffffu, w, (j0 + jj) & 31);
+        if (j0 + jj < nb && wj != 0.0f) {  // rows of empty splits are not added
+#pragma unroll
+          for (int c = 0; c < V; ++c) acc[c] += wj * x[jj][c];
         }
-        acc[r] = a;
       }
     }
   }
-  den = block_sum_128(den, s_red);
+  den = warp_sum(den);
   const float inv = den > 0.0f ? 1.0f / den : 0.0f;
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int d = tid + r * kCombineThreads;
-    if (d < head_dim) o[d] = acc[r] * inv;
-  }
+  for (int c = 0; c < V; ++c) o[lane + 32 * c] = acc[c] * inv;
 }
 
 // ===========================================================================
@@ -2160,11 +2147,11 @@ __global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t n_units = (int64_t)num_seqs * num_kv_heads * max_splits;
   const int64_t stride = gridDim.x;
+  if (blockIdx.x == 0)  // lengths beyond the table width, checked by all threads of CTA 0
+    for (int s = tid; s < num_seqs; s += C::kThreads)
+      if (max(seq_lens[s], 0) > covered_pages(seq_lens[s], BS, max_blocks_per_seq) * BS)
+        record_error(err, kDevSeqTooLong);
   if (tid == 0) {
-    if (blockIdx.x == 0)
-      for (int s = 0; s < num_seqs; ++s)
-        if (max(seq_lens[s], 0) > covered_pages(seq_lens[s], BS, max_blocks_per_seq) * BS)
-          record_error(err, kDevSeqTooLong);
     for (int i = 0; i < C::kStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
@@ -2721,6 +2708,27 @@ int dispatch_hg(const DecodeArgs& a, const Plan& p, float* wa, float2* wm, cudaS
   return kUnsupported;
 }
 
+// Launched right after the split kernel on the same stream.  (As a
+// programmatic dependent launch, whose CTAs wait in griddepcontrol.wait
+// until the split kernel is done, it measured 1-4% slower on B200.)
+cudaError_t launch_combine(const DecodeArgs& a, const Plan& p, const float* ws_acc,
+                           const float2* ws_ml, cudaStream_t stream) {
+  const int64_t pairs = (int64_t)a.num_seqs * a.num_heads;
+  const unsigned grid = (unsigned)((pairs + kCombineThreads / 32 - 1) / (kCombineThreads / 32));
+#define PKV_COMBINE_V(V)                                                                        \
+  case V:                                                                                      \
+    decode_combine_kernel<V><<<grid, kCombineThreads, 0, stream>>>(                            \
+        a.seq_lens, ws_acc, ws_ml, a.out, a.num_seqs, a.num_heads, a.block_size,               \
+        a.max_blocks_per_seq, p.pages_per_split, p.max_splits);                                \
+    return cudaGetLastError();
+  switch (a.head_dim / 32) {  // head_dim % 32 == 0 and <= 256 (launch checks)
+    PKV_COMBINE_V(1) PKV_COMBINE_V(2) PKV_COMBINE_V(3) PKV_COMBINE_V(4)
+    PKV_COMBINE_V(5) PKV_COMBINE_V(6) PKV_COMBINE_V(7) PKV_COMBINE_V(8)
+  }
+#undef PKV_COMBINE_V
+  return cudaErrorInvalidValue;
+}
+
 }  // namespace
 
 size_t decode_workspace_size(const DecodeArgs& a) {
@@ -2793,11 +2801,7 @@ int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
     return kCudaError;
   }
   // Splits > 1 and empty sequences are finished by the combine.
-  dim3 cgrid(a.num_seqs, a.num_heads);
-  decode_combine_kernel<<<cgrid, kCombineThreads, 0, stream>>>(a.seq_lens, ws_acc, ws_ml, a.out, a.num_heads,
-                                                   a.head_dim, a.block_size, a.max_blocks_per_seq,
-                                                   p.pages_per_split, p.max_splits);
-  e = cudaGetLastError();
+  e = launch_combine(a, p, ws_acc, ws_ml, stream);
   if (e != cudaSuccess) {
     set_error(std::string("combine launch failed: ") + cudaGetErrorString(e));
     return kCudaError;

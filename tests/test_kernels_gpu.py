@@ -342,14 +342,19 @@ def test_attention_stream_one_sequence_over_all_ctas(cuda):
         assert torch.equal(o, outs[0])
 
 
+@pytest.mark.parametrize("form", ["persistent", "split"])
 @pytest.mark.parametrize("group", [2, 4, 8])
 @pytest.mark.parametrize("pages", ["auto", "8", "16", "32"])
-def test_attention_tensor_core_gqa(cuda, monkeypatch, group, pages):
+def test_attention_tensor_core_gqa(cuda, monkeypatch, form, group, pages):
     """GQA groups of 2/4/8 query heads per KV head run on the tcgen05 kernel
     (q.K and p.V as int8 MMAs into tensor memory); ragged lengths, partial
-    128-token tiles, one to four tiles per split, several splits."""
+    128-token tiles, one to four tiles per split, several splits; the
+    persistent form (CTAs walk the units) and the split form (one CTA per
+    split), both followed by the combine kernel."""
     if pages != "auto":
         monkeypatch.setenv("PKV_DECODE_SPLIT_PAGES", pages)
+    if form == "split":
+        monkeypatch.setenv("PKV_DECODE_TC_SPLIT", "1")
     from pagedkv_fusion import _C
     for seed, S, hkv, L in ((31, 7, 4, 1500), (32, 3, 2, 130), (33, 12, 8, 700), (34, 2, 1, 17)):
         assert _C.quant_paged_attention_kernel_launches(S, group * hkv, hkv, 128, 16, 94) == 2
@@ -357,6 +362,37 @@ def test_attention_tensor_core_gqa(cuda, monkeypatch, group, pages):
                                               128, 16, L)
         args = quantized_problem(*prob)
         assert_attention_close(run_attention(args), c_oracle.paged_attention(*args))
+
+
+@pytest.mark.parametrize("group", [2, 4, 8])
+def test_tensor_core_persistent_merge_edges(cuda, group):
+    """The tensor-core path with its combine: sequences without pages (zero
+    output) and of one page, a long sequence with many splits whose units
+    wrap around the persistent grid, repeated calls bit for bit, and a
+    workspace of random bytes."""
+    r = np.random.default_rng(70 + group)
+    hkv = 2
+    q, k, v, bt, sl, sm = problems.make_paged_kv_problem(r, 6, group * hkv, hkv, 128, 16, 40000)
+    sl[1] = 0
+    sl[3] = min(int(sl[3]), 9)
+    args = quantized_problem(q, k, v, bt, sl, sm)
+    want = c_oracle.paged_attention(*args)
+    cuda.read_device_error(reset=True)
+    got = run_attention(args)
+    assert_attention_close(got, want)
+    assert float(got[1].abs().max()) == 0.0
+    assert torch.equal(got, run_attention(args))
+    S, H = q.shape[0], q.shape[1]
+    nbytes = cuda._attn_ws(S, H, hkv, 128, 16, bt.shape[1])
+    dargs = [dev(a) for a in args[:7]]
+    out = torch.empty_like(dargs[0])
+    ws = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda")
+    rc = cuda._attn(*(t.data_ptr() for t in dargs[:7]), out.data_ptr(), S, H, hkv, 128, 16,
+                    dargs[1].shape[0], bt.shape[1], float(sm), ws.data_ptr(), ws.numel(),
+                    torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert torch.equal(out, got)
+    assert cuda.read_device_error(reset=True) == 0
 
 
 def test_attention_tensor_core_matches_cuda_core_path(cuda, monkeypatch):
