@@ -232,8 +232,9 @@ __global__ void __launch_bounds__(kQThreads)
 // and, the parities of phases k-1 and k+1 being equal, pass it early) --
 // then warps 0-7 quantize the first block and warps 8-15 the second, one
 // head per warp.  A stage is refilled only after all 16 warps released it
-// (those not quantizing it right after their wait), so no warp can still be
-// waiting on a phase of a stage that has moved on.  Deep queues with few registers: the register kernel above
+// (those not quantizing it after their own block, with a wait of their own
+// on it), so no warp can still be waiting on a phase of a stage that has
+// moved on.  Deep queues with few registers: the register kernel above
 // keeps one block-head in flight per warp and its CTAs turn over every few
 // microseconds.
 constexpr int kBulkHalfWarps = 8;
@@ -362,21 +363,16 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
         ++cnt;
       }
     if (cnt == 0) break;
-    for (int i = 0; i < cnt; ++i) {  // every warp passes both phases, in order
-      const int st = (n + i) % kBulkStages;
-      if (live && !mbar_wait_bounded(&full[st], (uint32_t)((n + i) / kBulkStages) & 1u, err)) {
+    // The warps quantizing a block wait for it, quantize it and release it;
+    // then they wait for the pair's other block and release it, so a stage
+    // is refilled only after all 16 warps have passed its phase (and no
+    // block waits for its neighbour's arrival to start).
+    if (half < cnt) {
+      const int st = (n + half) % kBulkStages;
+      if (live && !mbar_wait_bounded(&full[st], (uint32_t)((n + half) / kBulkStages) & 1u, err)) {
         record_error(err, kDevWaitTimeout);
         live = false;
       }
-    }
-    // the other block of the pair is released at once by the warps not quantizing it
-    if (cnt == 2 || half == 1) {
-      const int other = cnt == 2 ? (n + (half ^ 1)) % kBulkStages : n % kBulkStages;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[other]);
-    }
-    if (half < cnt) {
-      const int st = (n + half) % kBulkStages;
       const int64_t blk_id = half ? second : first;
       const T* blk = reinterpret_cast<const T*>(smem_raw + st * block_bytes);
       if (live) {
@@ -399,6 +395,16 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
             *reinterpret_cast<uint32_t*>(out + t * tok) = quantize_word(f, sc, rcp, fast);
           }
         }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    if (cnt == 2 || half == 1) {  // the other block of the pair (the only one when cnt == 1)
+      const int i = cnt == 2 ? (half ^ 1) : 0;
+      const int st = (n + i) % kBulkStages;
+      if (live && !mbar_wait_bounded(&full[st], (uint32_t)((n + i) / kBulkStages) & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
