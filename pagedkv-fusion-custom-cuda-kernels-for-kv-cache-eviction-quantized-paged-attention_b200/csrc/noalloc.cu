@@ -130,9 +130,11 @@ int pkv_quant_paged_attention_noalloc(const float* q, const int8_t* k_cache,
       return PKV_ERR_CUDA;
     }
   }
-  // The scratch holds only split-K partials, each written by its split
-  // before the combine reads it within the same call, so nothing in it has
-  // to start at zero and the previous call's contents are harmless.
+  // The scratch holds split-K partials, each written by its split before it
+  // is merged within the same call, and the persistent decode kernel's
+  // arrival counters, which carry a per-launch tag (a counter left by an
+  // earlier call never matches).  Nothing in it has to start at zero, and
+  // the previous call's contents are harmless.
   return pkv_quant_paged_attention(q, k_cache, k_scale, v_cache, v_scale, block_tables,
                                    seq_lens, out, num_seqs, num_heads, num_kv_heads, head_dim,
                                    block_size, num_blocks, max_blocks_per_seq, sm_scale, scratch,
