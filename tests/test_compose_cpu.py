@@ -119,3 +119,16 @@ def test_attention_stats_definition_properties():
         assert a[b, t] >= 1 / 4 - 1e-7
     # a larger query sharpens the distribution: the mean weight drops
     assert O.attention_stats(k, q * 4, 1 / np.sqrt(128)).mean() < a.mean()
+
+
+def test_profile_driver_targets_and_no_device():
+    """The profiling driver (counterpart of the reference's
+    scripts/profile_kernels.py) knows the three targets and refuses to run
+    without a device instead of falling back to anything."""
+    import torch
+    from pagedkv_fusion import profile_kernels as pk
+    assert sorted(pk.KERNELS) == ["attention", "eviction", "quantize"]
+    if torch.cuda.is_available():
+        pytest.skip("a device is visible")
+    with pytest.raises(SystemExit):
+        pk.main(["attention", "--num-seqs", "2", "--seq-len", "64"])
