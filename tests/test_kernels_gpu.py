@@ -635,3 +635,34 @@ def test_eviction_plan_replays_match_eager(cuda):
         want = O.select_eviction_candidates(O.eviction_scores(*new), 2458)
         assert np.array_equal(idx.cpu().numpy(), want)
         assert np.array_equal(bits(scores), bits(O.eviction_scores(*new)))
+
+
+def test_eviction_8_cta_cluster_variant(cuda):
+    """The one-launch selection pinned to its 8-CTA cluster variant (the
+    cluster size is chosen once per process, so this runs in a fresh one):
+    scores and indices equal to the golden vectors at 16,384 blocks."""
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG, ROOT
+    code = r'''
+import numpy as np, torch
+from conftest import load_golden, sha
+from pagedkv_fusion import _C, problems
+ev = load_golden("eviction")
+for tag, kw in (("w16k", dict(mask="all")), ("w16k_ties", dict(mask="all", ties=True))):
+    rec, freq, att, msk = problems.eviction_problem(seed=0, **kw)
+    assert sha(rec, freq, att, msk) == str(ev[f"{tag}_digest"])
+    d = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (rec, freq, att, msk)]
+    for k in (1, 2458, 8192):
+        s, idx = _C.eviction_scores_select(*d, k)
+        assert np.array_equal(s.cpu().numpy().view(np.uint32), ev[f"{tag}_scores"].view(np.uint32))
+        assert np.array_equal(idx.cpu().numpy(), ev[f"{tag}_idx_k{k}"]), (tag, k)
+print("ok")
+'''
+    env = dict(os.environ, PKV_EVICTION_CLUSTER="8")
+    env["PYTHONPATH"] = os.pathsep.join([str(ROOT / "tests"), str(PKG), str(ROOT),
+                                         env.get("PYTHONPATH", "")])
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
