@@ -363,10 +363,24 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
         ++cnt;
       }
     if (cnt == 0) break;
-    // The warps quantizing a block wait for it, quantize it and release it;
-    // then they wait for the pair's other block and release it, so a stage
-    // is refilled only after all 16 warps have passed its phase (and no
-    // block waits for its neighbour's arrival to start).
+    // Every warp waits for both blocks of the pair and releases each after
+    // its wait, so a stage is refilled only after all 16 warps have passed
+    // its phase.  The warps quantizing the second block release the first
+    // before quantizing (it landed first), so its stage refills as soon as
+    // its own warps are done; the warps quantizing the first block do that
+    // first and only then wait for the second, so no block waits for its
+    // neighbour's arrival to start.
+    auto release_other = [&]() {  // the pair's other block (the only one when cnt == 1)
+      const int i = cnt == 2 ? (half ^ 1) : 0;
+      const int st = (n + i) % kBulkStages;
+      if (live && !mbar_wait_bounded(&full[st], (uint32_t)((n + i) / kBulkStages) & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    };
+    if (half == 1) release_other();
     if (half < cnt) {
       const int st = (n + half) % kBulkStages;
       if (live && !mbar_wait_bounded(&full[st], (uint32_t)((n + half) / kBulkStages) & 1u, err)) {
@@ -399,16 +413,7 @@ __global__ void __launch_bounds__(kBulkThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
-    if (cnt == 2 || half == 1) {  // the other block of the pair (the only one when cnt == 1)
-      const int i = cnt == 2 ? (half ^ 1) : 0;
-      const int st = (n + i) % kBulkStages;
-      if (live && !mbar_wait_bounded(&full[st], (uint32_t)((n + i) / kBulkStages) & 1u, err)) {
-        record_error(err, kDevWaitTimeout);
-        live = false;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-    }
+    if (half == 0 && cnt == 2) release_other();
     n += cnt;
   }
 }
