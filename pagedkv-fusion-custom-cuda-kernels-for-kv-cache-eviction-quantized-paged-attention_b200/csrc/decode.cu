@@ -2151,6 +2151,10 @@ __global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
     for (int s = tid; s < num_seqs; s += C::kThreads)
       if (max(seq_lens[s], 0) > covered_pages(seq_lens[s], BS, max_blocks_per_seq) * BS)
         record_error(err, kDevSeqTooLong);
+  // probability tiles: rows 3G..NQ-1 (MMA padding) are never written again
+  for (int i = tid; i < C::kMaxTiles * C::kRowBytes / 4; i += C::kThreads)
+    reinterpret_cast<uint32_t*>(s_p)[i] = 0u;
+  fence_proxy_async_smem();  // an MMA operand
   if (tid == 0) {
     for (int i = 0; i < C::kStages; ++i) {
       mbar_init(&full[i], 1);
@@ -2424,7 +2428,6 @@ __global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
           pt[sw128_offset(3 * g + 1, e)] = (uint8_t)((n >> 8) & 255u);
           pt[sw128_offset(3 * g + 2, e)] = (uint8_t)(n >> 16);
         }
-        for (int rw = 3 * G; rw < NQ; ++rw) pt[sw128_offset(rw, e)] = 0;
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
