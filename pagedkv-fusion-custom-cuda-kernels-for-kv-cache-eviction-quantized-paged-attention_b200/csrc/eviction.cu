@@ -18,7 +18,9 @@
 // merge steps between shared-memory passes.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <mutex>
 #include <string>
 
 #include "eviction_score.cuh"
@@ -140,6 +142,191 @@ __global__ void emit_kernel(const uint64_t* __restrict__ keys, int64_t k, int64_
   if (out_keys) out_keys[i] = key + (uint64_t)id_offset;
 }
 
+// ---------------------------------------------------------------------------
+// Radix prefilter for large selections.  Up to four passes over 16-bit
+// digits of the 64-bit keys (most significant first) find the prefix P of
+// the k-th smallest key: each pass histograms the digit of the keys whose
+// higher digits equal P, and a one-CTA scan appends the digit holding rank
+// k-1 to P.  The search stops as soon as the keys at or below P number at
+// most `cap` (keys are unique, so four digits always get there).  Those keys
+// -- the k smallest and possibly a few more -- are compacted and sorted, and
+// the first k emitted: the same output as sorting everything.  Keys strictly
+// below P fill the front of the candidate buffer (fewer than k of them) and
+// keys equal to P the rest, stopping at `cap`: a caller's merge keys with
+// more duplicates of the k-th key than fit still select exactly.
+// ---------------------------------------------------------------------------
+
+constexpr int kRadixBins = 1 << 16;
+constexpr int kRadixScanThreads = 1024;
+
+struct RadixState {
+  unsigned long long prefix;  // digits found so far
+  unsigned int below;         // keys below the prefix (their higher digits smaller)
+  unsigned int depth;         // digits in the prefix
+  unsigned int done;          // at most cap keys at or below the prefix
+  unsigned int n_below;       // keys below the prefix compacted so far
+  unsigned int n_equal;       // keys equal to the prefix compacted so far
+};
+static_assert(sizeof(RadixState) <= 256, "radix state outgrew its workspace slot");
+
+__global__ void __launch_bounds__(256)
+    radix_hist_kernel(const uint64_t* __restrict__ keys, int64_t n,
+                      const RadixState* __restrict__ st, unsigned int* __restrict__ hist,
+                      int pass) {
+  if (st->done) return;  // uniform
+  const int shift = 48 - 16 * pass;
+  const unsigned long long prefix = st->prefix;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t key = keys[i];
+    if ((key >> (shift + 16)) == prefix)  // pass >= 1: the first digit has its own kernel
+      atomicAdd(&hist[(key >> shift) & 0xFFFFu], 1u);
+  }
+}
+
+// First digit: every key counts, and uniform scores crowd a few hundred of
+// the 65,536 bins, where global atomics would serialise.  Each CTA counts
+// into shared memory instead -- two 16-bit counters per word, so the whole
+// histogram is 128 KB -- and flushes only its nonzero bins.  A CTA sees at
+// most kRadixHist0MaxKeys keys, so no 16-bit counter overflows.
+constexpr int kRadixHist0Threads = 1024;
+constexpr int kRadixHist0Keys = 63;  // keys per thread at most
+constexpr int64_t kRadixHist0MaxKeys = (int64_t)kRadixHist0Keys * kRadixHist0Threads;
+constexpr size_t kRadixHist0Smem = (kRadixBins / 2) * sizeof(unsigned int);
+static_assert(kRadixHist0MaxKeys < 65536, "16-bit shared counters could overflow");
+
+__global__ void __launch_bounds__(kRadixHist0Threads)
+    radix_hist0_kernel(const uint64_t* __restrict__ keys, int64_t n,
+                       unsigned int* __restrict__ hist) {
+  extern __shared__ uint4 s_hist4[];
+  unsigned int* s_hist = reinterpret_cast<unsigned int*>(s_hist4);
+  for (int w = threadIdx.x; w < kRadixBins / 8; w += kRadixHist0Threads)
+    s_hist4[w] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+  for (int64_t i = (int64_t)blockIdx.x * kRadixHist0Threads + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * kRadixHist0Threads) {
+    const unsigned int bin = (unsigned int)(keys[i] >> 48);
+    atomicAdd(&s_hist[bin >> 1], (bin & 1u) ? 0x10000u : 1u);
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < kRadixBins / 2; w += kRadixHist0Threads) {
+    const unsigned int v = s_hist[w];
+    if (v & 0xFFFFu) atomicAdd(&hist[2 * w], v & 0xFFFFu);
+    if (v >> 16) atomicAdd(&hist[2 * w + 1], v >> 16);
+  }
+}
+
+// Grid of radix_hist0_kernel: enough CTAs that none sees more than
+// kRadixHist0MaxKeys keys, at least one per SM.
+unsigned radix_hist0_grid(int64_t n) {
+  const int64_t per_pass = kRadixHist0MaxKeys;
+  const int64_t need = (n + per_pass - 1) / per_pass;
+  return (unsigned)std::max<int64_t>(need, 148);
+}
+
+bool radix_hist0_prepare() {
+  static bool ok[64];
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    ok[dev] = cudaFuncSetAttribute(radix_hist0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kRadixHist0Smem) == cudaSuccess;
+    cudaGetLastError();
+    done[dev] = true;
+  }
+  return ok[dev];
+}
+
+// One CTA: the bin holding rank k-1 among the keys counted, appended to the
+// prefix; the histogram is zeroed for the next pass.  The bins are read in
+// kRadixScanRounds coalesced rounds of four per thread (one uint4), each
+// round a block-wide scan on top of the previous rounds' total.
+constexpr int kRadixScanRounds = kRadixBins / (4 * kRadixScanThreads);
+
+__global__ void __launch_bounds__(kRadixScanThreads)
+    radix_scan_kernel(unsigned int* __restrict__ hist, RadixState* __restrict__ st, int64_t k,
+                      int64_t cap, int pass) {
+  __shared__ unsigned int s_warp[32];
+  __shared__ unsigned int s_total;
+  if (st->done) return;  // uniform
+  // read before the one writing thread below can change them
+  const unsigned int below = st->below;
+  const unsigned long long prefix = st->prefix;
+  const unsigned int target = (unsigned int)(k - 1) - below;  // rank among the counted keys
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint4* h4 = reinterpret_cast<uint4*>(hist);
+  constexpr int kAhead = 8;  // rounds loaded ahead of the scan
+  uint4 c[kAhead];
+#pragma unroll
+  for (int r = 0; r < kAhead; ++r) c[r] = h4[r * kRadixScanThreads + tid];
+  unsigned int carry = 0;  // keys in the rounds before this one
+#pragma unroll
+  for (int r = 0; r < kRadixScanRounds; ++r) {
+    const uint4 cur = c[r % kAhead];
+    if (r + kAhead < kRadixScanRounds) c[r % kAhead] = h4[(r + kAhead) * kRadixScanThreads + tid];
+    h4[r * kRadixScanThreads + tid] = make_uint4(0u, 0u, 0u, 0u);
+    const unsigned int cnt[4] = {cur.x, cur.y, cur.z, cur.w};
+    const unsigned int sum = cnt[0] + cnt[1] + cnt[2] + cnt[3];
+    unsigned int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const unsigned int w = s_warp[lane];
+      unsigned int x = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+      }
+      s_warp[lane] = x - w;  // exclusive prefix of warp totals
+      if (lane == 31) s_total = x;
+    }
+    __syncthreads();
+    unsigned int run = carry + s_warp[warp] + incl - sum;  // keys in bins before mine
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (run <= target && target < run + cnt[j]) {  // exactly one bin holds the rank
+        const unsigned int bin = (unsigned int)(r * 4 * kRadixScanThreads + 4 * tid + j);
+        st->prefix = (prefix << 16) | (unsigned long long)bin;
+        st->below = below + run;
+        st->depth = (unsigned int)pass + 1;
+        st->done = ((unsigned long long)below + run + cnt[j] <= (unsigned long long)cap ||
+                    pass == 3) ? 1u : 0u;
+      }
+      run += cnt[j];
+    }
+    carry += s_total;
+    __syncthreads();  // s_warp and s_total are rewritten next round
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    radix_compact_kernel(const uint64_t* __restrict__ keys, int64_t n, RadixState* __restrict__ st,
+                         uint64_t* __restrict__ cand, int64_t cap) {
+  const int shift = 64 - 16 * (int)st->depth;
+  const unsigned long long prefix = st->prefix;
+  const unsigned int below = st->below;  // < k <= cap
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t key = keys[i];
+    const unsigned long long p = key >> shift;
+    if (p < prefix) {
+      cand[atomicAdd(&st->n_below, 1u)] = key;
+    } else if (p == prefix) {
+      const unsigned int slot = below + atomicAdd(&st->n_equal, 1u);
+      if (slot < (unsigned long long)cap) cand[slot] = key;
+    }
+  }
+}
+
 // PKV_EVICTION_MULTI_KERNEL=1 selects the multi-kernel sort for every size
 // (used to cross-check the two paths).
 bool force_multi_kernel() {
@@ -179,6 +366,74 @@ int sort_keys(uint64_t* keys, int64_t n_pad, cudaStream_t stream) {
   return check_launch("bitonic sort");
 }
 
+// PKV_EVICTION_RADIX=0 turns the radix prefilter off (every selection then
+// sorts all keys); read once per process so the workspace sizes stay fixed.
+bool radix_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("PKV_EVICTION_RADIX");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
+// The radix prefilter pays off above 65,536 keys when the sorted
+// candidates (a power of two >= k + 1,024) are at most a quarter of them.
+int64_t radix_cap(int64_t n, int64_t k) {
+  if (n <= 65536 || k <= 0 || !radix_enabled()) return 0;
+  const int64_t cap = next_pow2(k + 1024);
+  return cap * 4 <= next_pow2(n) ? cap : 0;
+}
+
+// Workspace of the radix path after the n_pad keys: 16 bytes of alignment
+// slack, cap candidates, the histogram, the state.
+size_t radix_extra_bytes(int64_t cap) {
+  return 16 + (size_t)cap * sizeof(uint64_t) + kRadixBins * sizeof(unsigned int) + 256;
+}
+
+// keys[0 .. n) hold the keys (n_pad >= n of them); emits the k smallest,
+// ascending.  `extra` is the radix workspace when radix_cap(n, k) > 0.
+int select_sorted(uint64_t* keys, int64_t n, int64_t n_pad, int64_t k, int64_t id_offset,
+                  int64_t* out_ids, uint64_t* out_keys, uint8_t* extra, cudaStream_t stream) {
+  const int64_t cap = radix_cap(n, k);
+  uint64_t* sorted = keys;
+  if (cap > 0) {
+    extra = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(extra) + 15) & ~uintptr_t(15));
+    uint64_t* cand = reinterpret_cast<uint64_t*>(extra);  // cap * 8 bytes: hist stays 16-aligned
+    unsigned int* hist = reinterpret_cast<unsigned int*>(extra + cap * sizeof(uint64_t));
+    RadixState* st = reinterpret_cast<RadixState*>(extra + cap * sizeof(uint64_t) +
+                                                   kRadixBins * sizeof(unsigned int));
+    cudaError_t e = cudaMemsetAsync(hist, 0, kRadixBins * sizeof(unsigned int) + sizeof(RadixState),
+                                    stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(cand, 0xFF, cap * sizeof(uint64_t), stream);
+    if (e != cudaSuccess) {
+      set_error(std::string("eviction select reset failed: ") + cudaGetErrorString(e));
+      return kCudaError;
+    }
+    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(n, 256), 4 * 148);
+    if (!radix_hist0_prepare()) {
+      set_error("eviction select: radix histogram shared memory refused");
+      return kCudaError;
+    }
+    for (int pass = 0; pass < 4; ++pass) {
+      if (pass == 0)
+        radix_hist0_kernel<<<radix_hist0_grid(n), kRadixHist0Threads, kRadixHist0Smem, stream>>>(
+            keys, n, hist);
+      else
+        radix_hist_kernel<<<grid, 256, 0, stream>>>(keys, n, st, hist, pass);
+      radix_scan_kernel<<<1, kRadixScanThreads, 0, stream>>>(hist, st, k, cap, pass);
+    }
+    radix_compact_kernel<<<grid, 256, 0, stream>>>(keys, n, st, cand, cap);
+    const int rc = check_launch("eviction radix prefilter");
+    if (rc != kOk) return rc;
+    sorted = cand;
+    n_pad = cap;
+  }
+  int rc = sort_keys(sorted, n_pad, stream);
+  if (rc != kOk) return rc;
+  emit_kernel<<<blocks_for(k, 256), 256, 0, stream>>>(sorted, k, id_offset, out_ids, out_keys);
+  return check_launch("eviction emit");
+}
+
 }  // namespace
 
 int launch_eviction_scores(const float* recency, const float* frequency, const float* attn,
@@ -201,8 +456,9 @@ int launch_eviction_scores(const float* recency, const float* frequency, const f
 }
 
 size_t select_workspace_size(int64_t n, int64_t k) {
-  (void)k;
-  return (size_t)next_pow2(n < 2 ? 2 : n) * sizeof(uint64_t);
+  const size_t keys = (size_t)next_pow2(n < 2 ? 2 : n) * sizeof(uint64_t);
+  const int64_t cap = radix_cap(n, k < n ? k : n);
+  return cap > 0 ? keys + radix_extra_bytes(cap) : keys;
 }
 
 // Selections of at most 16,384 scores run in one cluster launch with no
@@ -226,16 +482,14 @@ int launch_select(const float* scores, const uint64_t* keys_in, int64_t n, int64
     if (rc != kUnsupported) return rc;
   }
   const int64_t n_pad = next_pow2(n);
-  if (workspace == nullptr || workspace_bytes < (size_t)n_pad * sizeof(uint64_t)) {
+  if (workspace == nullptr || workspace_bytes < select_workspace_size(n, k)) {
     set_error("workspace too small for eviction select");
     return kWorkspace;
   }
   uint64_t* keys = static_cast<uint64_t*>(workspace);
   make_keys_kernel<<<blocks_for(n_pad, 256), 256, 0, stream>>>(scores, keys_in, n, n_pad, keys);
-  int rc = sort_keys(keys, n_pad, stream);
-  if (rc != kOk) return rc;
-  emit_kernel<<<blocks_for(k, 256), 256, 0, stream>>>(keys, k, id_offset, out_ids, out_keys);
-  return check_launch("eviction emit");
+  return select_sorted(keys, n, n_pad, k, id_offset, out_ids, out_keys,
+                       static_cast<uint8_t*>(workspace) + n_pad * sizeof(uint64_t), stream);
 }
 
 size_t fused_select_workspace_size(int64_t n, int64_t k) {
@@ -260,7 +514,7 @@ int launch_scores_select(const float* recency, const float* frequency, const flo
     if (rc != kUnsupported) return rc;
   }
   const int64_t n_pad = next_pow2(num_blocks < 2 ? 2 : num_blocks);
-  if (k > 0 && (workspace == nullptr || workspace_bytes < (size_t)n_pad * sizeof(uint64_t))) {
+  if (k > 0 && (workspace == nullptr || workspace_bytes < select_workspace_size(num_blocks, k))) {
     set_error("workspace too small for fused eviction");
     return kWorkspace;
   }
@@ -278,10 +532,8 @@ int launch_scores_select(const float* recency, const float* frequency, const flo
                                                            block_size, w_r, w_f, w_a);
   int rc = check_launch("eviction score");
   if (rc != kOk || k <= 0) return rc;
-  rc = sort_keys(keys, n_pad, stream);
-  if (rc != kOk) return rc;
-  emit_kernel<<<blocks_for(k, 256), 256, 0, stream>>>(keys, k, 0, out_ids, nullptr);
-  return check_launch("eviction emit");
+  return select_sorted(keys, num_blocks, n_pad, k, 0, out_ids, nullptr,
+                       static_cast<uint8_t*>(workspace) + n_pad * sizeof(uint64_t), stream);
 }
 
 }  // namespace pkv

@@ -666,3 +666,41 @@ print("ok")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                        timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("dist", ["random", "grid_ties", "equal", "nan_neg_zero"])
+@pytest.mark.parametrize("n", [70001, 1_200_000])
+def test_select_large_radix_prefilter(cuda, dist, n):
+    """Selections above 65,536 blocks with k well below n take the radix
+    prefilter (the k-th key's prefix over up to four 16-bit digits, then only
+    the keys at or below it sorted): indices equal to the oracle's, order
+    included, through the scores path, the fused path and the merge path."""
+    r = np.random.default_rng(n + len(dist))
+    if dist == "random":
+        s = r.random(n).astype(np.float32)
+    elif dist == "grid_ties":
+        s = (np.floor(r.random(n) * 64) / 64).astype(np.float32)
+    elif dist == "equal":  # one key value: the prefix is found down to the block ids
+        s = np.full(n, 0.5, np.float32)
+    else:
+        s = r.standard_normal(n).astype(np.float32)
+        s[r.random(n) < 0.3] = np.nan
+        s[r.random(n) < 0.2] = -0.0
+        s[r.random(n) < 0.2] = 0.0
+    for k in sorted({1, 1000, n // 7, min(n // 5, 177_000)}):
+        want = O.select_eviction_candidates(s, k)
+        np.testing.assert_array_equal(cuda.eviction_select(dev(s), k).cpu().numpy(), want)
+    k = n // 7
+    want = O.select_eviction_candidates(s, k)
+    keys = (O.orderable_keys(s).astype(np.uint64) << np.uint64(32)) | np.arange(n, dtype=np.uint64)
+    np.testing.assert_array_equal(cuda.eviction_merge(dev(keys.view(np.int64)), k).cpu().numpy(),
+                                  want)
+    if dist == "random":  # fused scores + select on the same sizes
+        rec = r.random(n, dtype=np.float32)
+        freq = r.random(n, dtype=np.float32)
+        att = r.random((n, 16), dtype=np.float32)
+        msk = r.random((n, 16)) > 0.2
+        sc = O.eviction_scores(rec, freq, att, msk)
+        s2, idx = cuda.eviction_scores_select(dev(rec), dev(freq), dev(att), dev(msk), k)
+        np.testing.assert_array_equal(bits(s2), bits(sc))
+        np.testing.assert_array_equal(idx.cpu().numpy(), O.select_eviction_candidates(sc, k))
