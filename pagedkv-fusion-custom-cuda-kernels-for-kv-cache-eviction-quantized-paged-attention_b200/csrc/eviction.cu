@@ -115,6 +115,28 @@ __global__ void bitonic_global_step(uint64_t* __restrict__ keys, int64_t n_pad, 
   }
 }
 
+// Two global compare-exchange steps in one pass (strides s and s/2, both
+// >= tile): each thread owns the quad lo, lo + s/2, lo + s, lo + 3s/2,
+// which both steps touch only among themselves.  All four lie in one
+// 2s-aligned run, so they share the direction.
+__global__ void bitonic_global_step2(uint64_t* __restrict__ keys, int64_t n_pad, int64_t size,
+                                     int64_t s) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= n_pad / 4) return;
+  const int64_t h = s / 2;
+  const int64_t lo = 2 * s * (q / h) + (q % h);
+  const bool asc = (lo & size) == 0;
+  uint64_t a = keys[lo], b = keys[lo + h], c = keys[lo + s], d = keys[lo + s + h];
+  cas(a, c, asc);  // stride s
+  cas(b, d, asc);
+  cas(a, b, asc);  // stride s/2
+  cas(c, d, asc);
+  keys[lo] = a;
+  keys[lo + h] = b;
+  keys[lo + s] = c;
+  keys[lo + s + h] = d;
+}
+
 // Finishes merge size `size` for strides tile/2 .. 1 in shared memory.
 __global__ void __launch_bounds__(kTileThreads)
     bitonic_tile_merge(uint64_t* __restrict__ keys, int tile, int64_t size) {
@@ -308,22 +330,78 @@ __global__ void __launch_bounds__(kRadixScanThreads)
   }
 }
 
-__global__ void __launch_bounds__(256)
+// Compaction in chunks of kCompactThreads x kCompactPer keys: each CTA
+// reserves its chunk's slots with one atomic per class (below / equal), so
+// the two counters see a few thousand atomics instead of one per key.
+constexpr int kCompactThreads = 256;
+constexpr int kCompactPer = 4;
+
+__device__ __forceinline__ unsigned int warp_incl_scan(unsigned int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(kCompactThreads)
     radix_compact_kernel(const uint64_t* __restrict__ keys, int64_t n, RadixState* __restrict__ st,
                          uint64_t* __restrict__ cand, int64_t cap) {
+  constexpr int kWarps = kCompactThreads / 32;
+  constexpr int64_t kChunk = (int64_t)kCompactThreads * kCompactPer;
+  __shared__ unsigned int s_below[kWarps], s_equal[kWarps];
+  __shared__ unsigned int s_base[2];
   const int shift = 64 - 16 * (int)st->depth;
   const unsigned long long prefix = st->prefix;
   const unsigned int below = st->below;  // < k <= cap
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const uint64_t key = keys[i];
-    const unsigned long long p = key >> shift;
-    if (p < prefix) {
-      cand[atomicAdd(&st->n_below, 1u)] = key;
-    } else if (p == prefix) {
-      const unsigned int slot = below + atomicAdd(&st->n_equal, 1u);
-      if (slot < (unsigned long long)cap) cand[slot] = key;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t c0 = (int64_t)blockIdx.x * kChunk; c0 < n; c0 += (int64_t)gridDim.x * kChunk) {
+    uint64_t key[kCompactPer];
+    unsigned int cls = 0;  // 2 bits per key: 1 below, 2 equal
+    unsigned int nb = 0, ne = 0;
+#pragma unroll
+    for (int j = 0; j < kCompactPer; ++j) {
+      const int64_t i = c0 + (int64_t)j * kCompactThreads + tid;
+      key[j] = i < n ? keys[i] : 0ull;
+      const unsigned long long p = key[j] >> shift;
+      const unsigned int c = i >= n ? 0u : (p < prefix ? 1u : (p == prefix ? 2u : 0u));
+      cls |= c << (2 * j);
+      nb += c == 1u;
+      ne += c == 2u;
     }
+    const unsigned int ib = warp_incl_scan(nb, lane), ie = warp_incl_scan(ne, lane);
+    if (lane == 31) {
+      s_below[warp] = ib;
+      s_equal[warp] = ie;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      unsigned int tb = 0, te = 0;
+      for (int w = 0; w < kWarps; ++w) {
+        const unsigned int b = s_below[w], e = s_equal[w];
+        s_below[w] = tb;
+        s_equal[w] = te;
+        tb += b;
+        te += e;
+      }
+      s_base[0] = tb ? atomicAdd(&st->n_below, tb) : 0u;
+      s_base[1] = te ? atomicAdd(&st->n_equal, te) : 0u;
+    }
+    __syncthreads();
+    unsigned int ob = s_base[0] + s_below[warp] + ib - nb;
+    unsigned int oe = below + s_base[1] + s_equal[warp] + ie - ne;
+#pragma unroll
+    for (int j = 0; j < kCompactPer; ++j) {
+      const unsigned int c = (cls >> (2 * j)) & 3u;
+      if (c == 1u) {
+        cand[ob++] = key[j];
+      } else if (c == 2u) {
+        if (oe < (unsigned long long)cap) cand[oe] = key[j];
+        ++oe;
+      }
+    }
+    __syncthreads();  // the shared counters are rewritten next chunk
   }
 }
 
@@ -358,9 +436,17 @@ int sort_keys(uint64_t* keys, int64_t n_pad, cudaStream_t stream) {
   const size_t smem = (size_t)tile * sizeof(uint64_t);
   bitonic_tile_sort<<<(unsigned)(n_pad / tile), threads, smem, stream>>>(keys, tile);
   for (int64_t size = (int64_t)tile * 2; size <= n_pad; size <<= 1) {
-    for (int64_t stride = size / 2; stride >= tile; stride >>= 1)
-      bitonic_global_step<<<blocks_for(n_pad / 2, 256), 256, 0, stream>>>(keys, n_pad, size,
-                                                                           stride);
+    for (int64_t stride = size / 2; stride >= tile;) {
+      if (stride / 2 >= tile) {
+        bitonic_global_step2<<<blocks_for(n_pad / 4, 256), 256, 0, stream>>>(keys, n_pad, size,
+                                                                              stride);
+        stride >>= 2;
+      } else {
+        bitonic_global_step<<<blocks_for(n_pad / 2, 256), 256, 0, stream>>>(keys, n_pad, size,
+                                                                             stride);
+        stride >>= 1;
+      }
+    }
     bitonic_tile_merge<<<(unsigned)(n_pad / tile), threads, smem, stream>>>(keys, tile, size);
   }
   return check_launch("bitonic sort");
@@ -422,7 +508,9 @@ int select_sorted(uint64_t* keys, int64_t n, int64_t n_pad, int64_t k, int64_t i
         radix_hist_kernel<<<grid, 256, 0, stream>>>(keys, n, st, hist, pass);
       radix_scan_kernel<<<1, kRadixScanThreads, 0, stream>>>(hist, st, k, cap, pass);
     }
-    radix_compact_kernel<<<grid, 256, 0, stream>>>(keys, n, st, cand, cap);
+    radix_compact_kernel<<<(unsigned)std::min<int64_t>(
+                               blocks_for(n, kCompactThreads * kCompactPer), 4 * 148),
+                           kCompactThreads, 0, stream>>>(keys, n, st, cand, cap);
     const int rc = check_launch("eviction radix prefilter");
     if (rc != kOk) return rc;
     sorted = cand;
