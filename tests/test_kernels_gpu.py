@@ -704,3 +704,36 @@ def test_select_large_radix_prefilter(cuda, dist, n):
         s2, idx = cuda.eviction_scores_select(dev(rec), dev(freq), dev(att), dev(msk), k)
         np.testing.assert_array_equal(bits(s2), bits(sc))
         np.testing.assert_array_equal(idx.cpu().numpy(), O.select_eviction_candidates(sc, k))
+
+
+def test_select_without_radix_prefilter(cuda):
+    """PKV_EVICTION_RADIX=0 (read once per process, so in a fresh one):
+    selections above 65,536 blocks sort every key instead; indices equal
+    to the oracle's, scores and merge paths."""
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG, ROOT
+    code = r'''
+import numpy as np, torch
+from oracle import oracle as O
+from pagedkv_fusion import _C
+r = np.random.default_rng(3)
+n = 140001
+s = (np.floor(r.random(n) * 256) / 256).astype(np.float32)
+s[r.random(n) < 0.1] = np.nan
+d = torch.from_numpy(s).cuda()
+assert _C._select_ws(n, 1000) == (1 << 18) * 8  # the sort keys only
+for k in (1, 1000, 20000):
+    assert np.array_equal(_C.eviction_select(d, k).cpu().numpy(), O.select_eviction_candidates(s, k)), k
+keys = (O.orderable_keys(s).astype(np.uint64) << np.uint64(32)) | np.arange(n, dtype=np.uint64)
+got = _C.eviction_merge(torch.from_numpy(keys.view(np.int64)).cuda(), 20000).cpu().numpy()
+assert np.array_equal(got, O.select_eviction_candidates(s, 20000))
+print("ok")
+'''
+    env = dict(os.environ, PKV_EVICTION_RADIX="0")
+    env["PYTHONPATH"] = os.pathsep.join([str(ROOT / "tests"), str(PKG), str(ROOT),
+                                         env.get("PYTHONPATH", "")])
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
