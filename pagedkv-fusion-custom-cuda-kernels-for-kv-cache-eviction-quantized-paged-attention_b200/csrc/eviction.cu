@@ -101,6 +101,110 @@ __global__ void __launch_bounds__(kTileThreads)
   for (int i = threadIdx.x; i < tile; i += blockDim.x) keys[base + i] = s[i];
 }
 
+// Register form of the tile kernels: a warp holds 128 consecutive keys of
+// the tile, key j of a thread at tile index warp * 128 + 32 * j + lane.
+// Strides 64 and 32 pair a thread's own keys, strides 16 .. 1 pair lanes
+// (shuffles); only strides >= 128 go through shared memory, so a 4,096-key
+// tile sort takes 25 block barriers instead of 78.
+constexpr int kWarpKeys = 128;
+
+__device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int m) {
+  const unsigned int lo = __shfl_xor_sync(0xffffffffu, (unsigned int)v, m);
+  const unsigned int hi = __shfl_xor_sync(0xffffffffu, (unsigned int)(v >> 32), m);
+  return ((uint64_t)hi << 32) | lo;
+}
+
+// Steps of strides top .. 1 (top <= 64) of merge size `size`; g0 is the
+// global index of the thread's key 0.
+__device__ __forceinline__ void bitonic_reg_steps(uint64_t (&v)[4], int64_t g0, int64_t size,
+                                                  int top, int lane) {
+  if (top >= 64) {
+    cas(v[0], v[2], (g0 & size) == 0);
+    cas(v[1], v[3], ((g0 + 32) & size) == 0);
+  }
+  if (top >= 32) {
+    cas(v[0], v[1], (g0 & size) == 0);
+    cas(v[2], v[3], ((g0 + 64) & size) == 0);
+  }
+  for (int st = top < 16 ? top : 16; st >= 1; st >>= 1) {
+    const bool lower = (lane & st) == 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint64_t y = shfl_xor_u64(v[j], st);
+      const bool asc = ((g0 + 32 * j) & size) == 0;
+      const bool take_min = lower == asc;
+      v[j] = take_min ? (y < v[j] ? y : v[j]) : (y > v[j] ? y : v[j]);
+    }
+  }
+}
+
+// bitonic_tile_sort for tiles of at least 128 keys, tile / 4 threads.
+__global__ void __launch_bounds__(kTileThreads)
+    bitonic_tile_sort_reg(uint64_t* __restrict__ keys, int tile) {
+  extern __shared__ uint64_t s[];
+  const int64_t base = (int64_t)blockIdx.x * tile;
+  const int lane = threadIdx.x & 31;
+  const int t0 = (threadIdx.x >> 5) * kWarpKeys + lane;
+  const int64_t g0 = base + t0;
+  uint64_t v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = keys[g0 + 32 * j];
+  for (int size = 2; size <= kWarpKeys && size <= tile; size <<= 1)
+    bitonic_reg_steps(v, g0, size, size / 2, lane);
+  if (tile > kWarpKeys) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[t0 + 32 * j] = v[j];
+    __syncthreads();
+    for (int size = 2 * kWarpKeys; size <= tile; size <<= 1) {
+      for (int stride = size >> 1; stride >= kWarpKeys; stride >>= 1) {
+        for (int p = threadIdx.x; p < tile / 2; p += blockDim.x) {
+          const int lo = 2 * stride * (p / stride) + (p % stride);
+          cas(s[lo], s[lo + stride], ((base + lo) & size) == 0);
+        }
+        __syncthreads();
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = s[t0 + 32 * j];
+      bitonic_reg_steps(v, g0, size, kWarpKeys / 2, lane);
+      if (size < tile) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[t0 + 32 * j] = v[j];
+        __syncthreads();
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) keys[g0 + 32 * j] = v[j];
+}
+
+// Finishes merge size `size` (> tile) for strides tile/2 .. 1: the
+// shared-memory strides, then the register ones (tile of at least 256 keys,
+// tile / 4 threads).
+__global__ void __launch_bounds__(kTileThreads)
+    bitonic_tile_merge_reg(uint64_t* __restrict__ keys, int tile, int64_t size) {
+  extern __shared__ uint64_t s[];
+  const int64_t base = (int64_t)blockIdx.x * tile;
+  for (int i = threadIdx.x; i < tile; i += blockDim.x) s[i] = keys[base + i];
+  __syncthreads();
+  const bool asc = (base & size) == 0;
+  for (int stride = tile >> 1; stride >= kWarpKeys; stride >>= 1) {
+    for (int p = threadIdx.x; p < tile / 2; p += blockDim.x) {
+      const int lo = 2 * stride * (p / stride) + (p % stride);
+      cas(s[lo], s[lo + stride], asc);
+    }
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31;
+  const int t0 = (threadIdx.x >> 5) * kWarpKeys + lane;
+  const int64_t g0 = base + t0;
+  uint64_t v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = s[t0 + 32 * j];
+  bitonic_reg_steps(v, g0, size, kWarpKeys / 2, lane);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) keys[g0 + 32 * j] = v[j];
+}
+
 // One global compare-exchange step (stride >= tile).
 __global__ void bitonic_global_step(uint64_t* __restrict__ keys, int64_t n_pad, int64_t size,
                                     int64_t stride) {
@@ -135,24 +239,6 @@ __global__ void bitonic_global_step2(uint64_t* __restrict__ keys, int64_t n_pad,
   keys[lo + h] = b;
   keys[lo + s] = c;
   keys[lo + s + h] = d;
-}
-
-// Finishes merge size `size` for strides tile/2 .. 1 in shared memory.
-__global__ void __launch_bounds__(kTileThreads)
-    bitonic_tile_merge(uint64_t* __restrict__ keys, int tile, int64_t size) {
-  extern __shared__ uint64_t s[];
-  const int64_t base = (int64_t)blockIdx.x * tile;
-  for (int i = threadIdx.x; i < tile; i += blockDim.x) s[i] = keys[base + i];
-  __syncthreads();
-  const bool asc = (base & size) == 0;
-  for (int stride = tile >> 1; stride > 0; stride >>= 1) {
-    for (int p = threadIdx.x; p < tile / 2; p += blockDim.x) {
-      const int lo = 2 * stride * (p / stride) + (p % stride);
-      cas(s[lo], s[lo + stride], asc);
-    }
-    __syncthreads();
-  }
-  for (int i = threadIdx.x; i < tile; i += blockDim.x) keys[base + i] = s[i];
 }
 
 __global__ void emit_kernel(const uint64_t* __restrict__ keys, int64_t k, int64_t id_offset,
@@ -434,7 +520,11 @@ int sort_keys(uint64_t* keys, int64_t n_pad, cudaStream_t stream) {
   const int tile = (int)(n_pad < kTile ? n_pad : kTile);
   const int threads = tile / 2 < kTileThreads ? tile / 2 : kTileThreads;
   const size_t smem = (size_t)tile * sizeof(uint64_t);
-  bitonic_tile_sort<<<(unsigned)(n_pad / tile), threads, smem, stream>>>(keys, tile);
+  static_assert(kTile / 4 == kTileThreads, "register tile kernels: four keys per thread");
+  if (tile >= kWarpKeys)
+    bitonic_tile_sort_reg<<<(unsigned)(n_pad / tile), tile / 4, smem, stream>>>(keys, tile);
+  else
+    bitonic_tile_sort<<<(unsigned)(n_pad / tile), threads, smem, stream>>>(keys, tile);
   for (int64_t size = (int64_t)tile * 2; size <= n_pad; size <<= 1) {
     for (int64_t stride = size / 2; stride >= tile;) {
       if (stride / 2 >= tile) {
@@ -447,7 +537,7 @@ int sort_keys(uint64_t* keys, int64_t n_pad, cudaStream_t stream) {
         stride >>= 1;
       }
     }
-    bitonic_tile_merge<<<(unsigned)(n_pad / tile), threads, smem, stream>>>(keys, tile, size);
+    bitonic_tile_merge_reg<<<(unsigned)(n_pad / tile), tile / 4, smem, stream>>>(keys, tile, size);
   }
   return check_launch("bitonic sort");
 }
