@@ -274,22 +274,44 @@ struct RadixState {
   unsigned int done;          // at most cap keys at or below the prefix
   unsigned int n_below;       // keys below the prefix compacted so far
   unsigned int n_equal;       // keys equal to the prefix compacted so far
+  unsigned int arrived;       // CTAs of the current histogram pass that finished
 };
 static_assert(sizeof(RadixState) <= 256, "radix state outgrew its workspace slot");
 
-__global__ void __launch_bounds__(256)
-    radix_hist_kernel(const uint64_t* __restrict__ keys, int64_t n,
-                      const RadixState* __restrict__ st, unsigned int* __restrict__ hist,
-                      int pass) {
+__device__ void radix_scan_block(unsigned int* __restrict__ hist, RadixState* __restrict__ st,
+                                 int64_t k, int64_t cap, int pass);
+
+// End of a histogram pass (blocks of kRadixScanThreads threads): the last CTA
+// to finish runs the scan.  Every CTA fences its counts before it arrives,
+// so the last one reads the complete histogram from L2.  No CTA waits.
+__device__ __forceinline__ void radix_scan_if_last(unsigned int* __restrict__ hist,
+                                                   RadixState* __restrict__ st, int64_t k,
+                                                   int64_t cap, int pass) {
+  __shared__ unsigned int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&st->arrived, 1u) == gridDim.x - 1 ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;  // uniform
+  __threadfence();
+  radix_scan_block(hist, st, k, cap, pass);
+  if (threadIdx.x == 0) st->arrived = 0u;  // for the next pass's kernel
+}
+
+// Digits 2-4 (pass >= 1): only keys whose higher digits equal the prefix
+// count; returns at once when an earlier pass already stopped the search.
+__global__ void __launch_bounds__(kRadixScanThreads)
+    radix_hist_kernel(const uint64_t* __restrict__ keys, int64_t n, RadixState* __restrict__ st,
+                      unsigned int* __restrict__ hist, int64_t k, int64_t cap, int pass) {
   if (st->done) return;  // uniform
   const int shift = 48 - 16 * pass;
   const unsigned long long prefix = st->prefix;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const uint64_t key = keys[i];
-    if ((key >> (shift + 16)) == prefix)  // pass >= 1: the first digit has its own kernel
-      atomicAdd(&hist[(key >> shift) & 0xFFFFu], 1u);
+    if ((key >> (shift + 16)) == prefix) atomicAdd(&hist[(key >> shift) & 0xFFFFu], 1u);
   }
+  radix_scan_if_last(hist, st, k, cap, pass);
 }
 
 // First digit: every key counts, and uniform scores crowd a few hundred of
@@ -304,8 +326,8 @@ constexpr size_t kRadixHist0Smem = (kRadixBins / 2) * sizeof(unsigned int);
 static_assert(kRadixHist0MaxKeys < 65536, "16-bit shared counters could overflow");
 
 __global__ void __launch_bounds__(kRadixHist0Threads)
-    radix_hist0_kernel(const uint64_t* __restrict__ keys, int64_t n,
-                       unsigned int* __restrict__ hist) {
+    radix_hist0_kernel(const uint64_t* __restrict__ keys, int64_t n, RadixState* __restrict__ st,
+                       unsigned int* __restrict__ hist, int64_t k, int64_t cap) {
   extern __shared__ uint4 s_hist4[];
   unsigned int* s_hist = reinterpret_cast<unsigned int*>(s_hist4);
   for (int w = threadIdx.x; w < kRadixBins / 8; w += kRadixHist0Threads)
@@ -322,6 +344,7 @@ __global__ void __launch_bounds__(kRadixHist0Threads)
     if (v & 0xFFFFu) atomicAdd(&hist[2 * w], v & 0xFFFFu);
     if (v >> 16) atomicAdd(&hist[2 * w + 1], v >> 16);
   }
+  radix_scan_if_last(hist, st, k, cap, 0);
 }
 
 // Grid of radix_hist0_kernel: enough CTAs that none sees more than
@@ -348,15 +371,17 @@ bool radix_hist0_prepare() {
   return ok[dev];
 }
 
-// One CTA: the bin holding rank k-1 among the keys counted, appended to the
-// prefix; the histogram is zeroed for the next pass.  The bins are read in
+// One CTA (the last of a histogram pass): the bin holding rank k-1 among the
+// keys counted, appended to the prefix; the histogram is zeroed for the next
+// pass.  The bins are read in
 // kRadixScanRounds coalesced rounds of four per thread (one uint4), each
 // round a block-wide scan on top of the previous rounds' total.
 constexpr int kRadixScanRounds = kRadixBins / (4 * kRadixScanThreads);
 
-__global__ void __launch_bounds__(kRadixScanThreads)
-    radix_scan_kernel(unsigned int* __restrict__ hist, RadixState* __restrict__ st, int64_t k,
-                      int64_t cap, int pass) {
+__device__ __noinline__ void radix_scan_block(unsigned int* __restrict__ hist,
+                                              RadixState* __restrict__ st, int64_t k, int64_t cap,
+                                              int pass) {
+  static_assert(kRadixHist0Threads == kRadixScanThreads, "the scan runs in a histogram CTA");
   __shared__ unsigned int s_warp[32];
   __shared__ unsigned int s_total;
   if (st->done) return;  // uniform
@@ -369,12 +394,13 @@ __global__ void __launch_bounds__(kRadixScanThreads)
   constexpr int kAhead = 8;  // rounds loaded ahead of the scan
   uint4 c[kAhead];
 #pragma unroll
-  for (int r = 0; r < kAhead; ++r) c[r] = h4[r * kRadixScanThreads + tid];
+  for (int r = 0; r < kAhead; ++r) c[r] = __ldcg(&h4[r * kRadixScanThreads + tid]);
   unsigned int carry = 0;  // keys in the rounds before this one
 #pragma unroll
   for (int r = 0; r < kRadixScanRounds; ++r) {
     const uint4 cur = c[r % kAhead];
-    if (r + kAhead < kRadixScanRounds) c[r % kAhead] = h4[(r + kAhead) * kRadixScanThreads + tid];
+    if (r + kAhead < kRadixScanRounds)
+      c[r % kAhead] = __ldcg(&h4[(r + kAhead) * kRadixScanThreads + tid]);
     h4[r * kRadixScanThreads + tid] = make_uint4(0u, 0u, 0u, 0u);
     const unsigned int cnt[4] = {cur.x, cur.y, cur.z, cur.w};
     const unsigned int sum = cnt[0] + cnt[1] + cnt[2] + cnt[3];
@@ -552,10 +578,11 @@ bool radix_enabled() {
   return on;
 }
 
-// The radix prefilter pays off above 65,536 keys when the sorted
+// The radix prefilter pays off above kRadixMinKeys keys when the sorted
 // candidates (a power of two >= k + 1,024) are at most a quarter of them.
+constexpr int64_t kRadixMinKeys = 16384;
 int64_t radix_cap(int64_t n, int64_t k) {
-  if (n <= 65536 || k <= 0 || !radix_enabled()) return 0;
+  if (n <= kRadixMinKeys || k <= 0 || !radix_enabled()) return 0;
   const int64_t cap = next_pow2(k + 1024);
   return cap * 4 <= next_pow2(n) ? cap : 0;
 }
@@ -585,19 +612,16 @@ int select_sorted(uint64_t* keys, int64_t n, int64_t n_pad, int64_t k, int64_t i
       set_error(std::string("eviction select reset failed: ") + cudaGetErrorString(e));
       return kCudaError;
     }
-    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(n, 256), 4 * 148);
+    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(n, kRadixScanThreads), 2 * 148);
     if (!radix_hist0_prepare()) {
       set_error("eviction select: radix histogram shared memory refused");
       return kCudaError;
     }
-    for (int pass = 0; pass < 4; ++pass) {
-      if (pass == 0)
-        radix_hist0_kernel<<<radix_hist0_grid(n), kRadixHist0Threads, kRadixHist0Smem, stream>>>(
-            keys, n, hist);
-      else
-        radix_hist_kernel<<<grid, 256, 0, stream>>>(keys, n, st, hist, pass);
-      radix_scan_kernel<<<1, kRadixScanThreads, 0, stream>>>(hist, st, k, cap, pass);
-    }
+    // each pass ends with the scan in its last CTA
+    radix_hist0_kernel<<<radix_hist0_grid(n), kRadixHist0Threads, kRadixHist0Smem, stream>>>(
+        keys, n, st, hist, k, cap);
+    for (int pass = 1; pass < 4; ++pass)
+      radix_hist_kernel<<<grid, kRadixScanThreads, 0, stream>>>(keys, n, st, hist, k, cap, pass);
     radix_compact_kernel<<<(unsigned)std::min<int64_t>(
                                blocks_for(n, kCompactThreads * kCompactPer), 4 * 148),
                            kCompactThreads, 0, stream>>>(keys, n, st, cand, cap);

@@ -132,12 +132,11 @@ def test_select_workspace_is_padded_key_array(lib):
     f.argtypes = [ct.c_int64, ct.c_int64]
     f.restype = ct.c_size_t
     assert f(16384, 2458) == 16384 * 8
-    assert f(16385, 1) == 32768 * 8
-    assert f(65536, 1) == 65536 * 8
+    assert f(16385, 8000) == 32768 * 8  # no radix prefilter: k too large
 
 
-def test_select_workspace_adds_radix_prefilter_above_64k(lib):
-    """Above 65,536 blocks, when next_pow2(k + 1024) candidates are at most a
+def test_select_workspace_adds_radix_prefilter_above_16k(lib):
+    """Above 16,384 blocks, when next_pow2(k + 1024) candidates are at most a
     quarter of the padded keys, the workspace adds 16 bytes of alignment
     slack, the candidate buffer, a 65,536-bin histogram and a 256-byte
     state; otherwise it stays the padded key array."""
@@ -152,6 +151,9 @@ def test_select_workspace_adds_radix_prefilter_above_64k(lib):
     assert f(1_200_000, 177_000) == keys + 16 + (1 << 18) * 8 + 65536 * 4 + 256
     assert f(1_200_000, 600_000) == keys  # candidates would exceed a quarter
     assert f(70001, 10000) == (1 << 17) * 8 + 16 + 16384 * 8 + 65536 * 4 + 256
+    assert f(20000, 1000) == (1 << 15) * 8 + 16 + 2048 * 8 + 65536 * 4 + 256
+    assert f(20000, 8000) == (1 << 15) * 8  # 16,384 candidates: half the keys
+    assert f(16384, 1) == 16384 * 8  # the one-launch cluster range
 
 
 def test_shim_imports_and_rejects_host_tensors():

@@ -669,9 +669,9 @@ print("ok")
 
 
 @pytest.mark.parametrize("dist", ["random", "grid_ties", "equal", "nan_neg_zero"])
-@pytest.mark.parametrize("n", [70001, 1_200_000])
+@pytest.mark.parametrize("n", [20000, 70001, 1_200_000])
 def test_select_large_radix_prefilter(cuda, dist, n):
-    """Selections above 65,536 blocks with k well below n take the radix
+    """Selections above 16,384 blocks with k well below n take the radix
     prefilter (the k-th key's prefix over up to four 16-bit digits, then only
     the keys at or below it sorted): indices equal to the oracle's, order
     included, through the scores path, the fused path and the merge path."""
@@ -708,7 +708,7 @@ def test_select_large_radix_prefilter(cuda, dist, n):
 
 def test_select_without_radix_prefilter(cuda):
     """PKV_EVICTION_RADIX=0 (read once per process, so in a fresh one):
-    selections above 65,536 blocks sort every key instead; indices equal
+    selections above 16,384 blocks sort every key instead; indices equal
     to the oracle's, scores and merge paths."""
     import os
     import subprocess
