@@ -579,12 +579,17 @@ bool radix_enabled() {
 }
 
 // The radix prefilter pays off above kRadixMinKeys keys when the sorted
-// candidates (a power of two >= k + 1,024) are at most a quarter of them.
+// candidates (a power of two >= k + 1,024) are a small enough part of the
+// padded keys: an eighth up to 2^16 padded keys, a quarter below 2^20, half
+// from 2^20 on (where each merge level the full sort adds costs more than
+// the prefilter's passes).
 constexpr int64_t kRadixMinKeys = 16384;
 int64_t radix_cap(int64_t n, int64_t k) {
   if (n <= kRadixMinKeys || k <= 0 || !radix_enabled()) return 0;
   const int64_t cap = next_pow2(k + 1024);
-  return cap * 4 <= next_pow2(n) ? cap : 0;
+  const int64_t n_pad = next_pow2(n);
+  const int64_t ratio = n_pad >= (int64_t(1) << 20) ? 2 : (n_pad > 65536 ? 4 : 8);
+  return cap * ratio <= n_pad ? cap : 0;
 }
 
 // Workspace of the radix path after the n_pad keys: 16 bytes of alignment

@@ -136,10 +136,11 @@ def test_select_workspace_is_padded_key_array(lib):
 
 
 def test_select_workspace_adds_radix_prefilter_above_16k(lib):
-    """Above 16,384 blocks, when next_pow2(k + 1024) candidates are at most a
-    quarter of the padded keys, the workspace adds 16 bytes of alignment
-    slack, the candidate buffer, a 65,536-bin histogram and a 256-byte
-    state; otherwise it stays the padded key array."""
+    """Above 16,384 blocks, when next_pow2(k + 1024) candidates are at most
+    an eighth of the padded keys (a quarter above 2^16 padded keys, half
+    from 2^20 on), the workspace adds 16 bytes of alignment slack, the candidate buffer, a
+    65,536-bin histogram and a 256-byte state; otherwise it stays the padded
+    key array."""
     import os
     f = lib.pkv_eviction_select_workspace_size
     f.argtypes = [ct.c_int64, ct.c_int64]
@@ -149,10 +150,15 @@ def test_select_workspace_adds_radix_prefilter_above_16k(lib):
         pytest.skip("radix prefilter switched off in this environment")
     assert f(1_200_000, 1000) == keys + 16 + 2048 * 8 + 65536 * 4 + 256
     assert f(1_200_000, 177_000) == keys + 16 + (1 << 18) * 8 + 65536 * 4 + 256
-    assert f(1_200_000, 600_000) == keys  # candidates would exceed a quarter
+    # half of the padded keys: prefiltered from 2^20 padded keys on
+    assert f(1_200_000, 600_000) == keys + 16 + (1 << 20) * 8 + 65536 * 4 + 256
+    assert f(354_000, 177_000) == (1 << 19) * 8
+    assert f(1_200_000, 1_100_000) == keys  # candidates = all the padded keys
     assert f(70001, 10000) == (1 << 17) * 8 + 16 + 16384 * 8 + 65536 * 4 + 256
     assert f(20000, 1000) == (1 << 15) * 8 + 16 + 2048 * 8 + 65536 * 4 + 256
     assert f(20000, 8000) == (1 << 15) * 8  # 16,384 candidates: half the keys
+    assert f(40000, 12000) == (1 << 16) * 8  # a quarter, at 2^16 padded keys
+    assert f(300_000, 100_000) == (1 << 19) * 8 + 16 + (1 << 17) * 8 + 65536 * 4 + 256
     assert f(16384, 1) == 16384 * 8  # the one-launch cluster range
 
 

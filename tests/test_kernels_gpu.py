@@ -687,7 +687,7 @@ def test_select_large_radix_prefilter(cuda, dist, n):
         s[r.random(n) < 0.3] = np.nan
         s[r.random(n) < 0.2] = -0.0
         s[r.random(n) < 0.2] = 0.0
-    for k in sorted({1, 1000, n // 7, min(n // 5, 177_000)}):
+    for k in sorted({1, 1000, n // 7, min(n // 5, 177_000), n // 2}):
         want = O.select_eviction_candidates(s, k)
         np.testing.assert_array_equal(cuda.eviction_select(dev(s), k).cpu().numpy(), want)
     k = n // 7
