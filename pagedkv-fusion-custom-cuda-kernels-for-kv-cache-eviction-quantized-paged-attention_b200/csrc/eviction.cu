@@ -254,9 +254,10 @@ __global__ void emit_kernel(const uint64_t* __restrict__ keys, int64_t k, int64_
 // Radix prefilter for large selections.  Up to four passes over 16-bit
 // digits of the 64-bit keys (most significant first) find the prefix P of
 // the k-th smallest key: each pass histograms the digit of the keys whose
-// higher digits equal P, and a one-CTA scan appends the digit holding rank
-// k-1 to P.  The search stops as soon as the keys at or below P number at
-// most `cap` (keys are unique, so four digits always get there).  Those keys
+// higher digits equal P, and the pass's last CTA appends the digit holding
+// rank k-1 to P.  The search stops as soon as the keys at or below P number
+// at most `cap` (for unique keys four digits always get there; the fourth
+// pass stops it regardless).  Those keys
 // -- the k smallest and possibly a few more -- are compacted and sorted, and
 // the first k emitted: the same output as sorting everything.  Keys strictly
 // below P fill the front of the candidate buffer (fewer than k of them) and
