@@ -70,8 +70,8 @@ __global__ void make_keys_kernel(const float* __restrict__ scores,
 // n_pad) is ascending everywhere.
 // ---------------------------------------------------------------------------
 
-constexpr int kTile = 4096;  // keys per shared-memory tile (32 KB)
-constexpr int kTileThreads = 1024;
+constexpr int kTile = 2048;  // keys per shared-memory tile (16 KB)
+constexpr int kTileThreads = 512;
 
 __device__ __forceinline__ void cas(uint64_t& a, uint64_t& b, bool asc) {
   if ((a > b) == asc) {
