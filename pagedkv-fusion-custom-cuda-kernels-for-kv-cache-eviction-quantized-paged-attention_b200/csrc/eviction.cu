@@ -101,6 +101,31 @@ __global__ void __launch_bounds__(kTileThreads)
   for (int i = threadIdx.x; i < tile; i += blockDim.x) keys[base + i] = s[i];
 }
 
+// Three global steps in one pass (strides s, s/2, s/4, all >= tile): each
+// thread owns the eight keys lo + a * s/4 (a = 0 .. 7), closed under the
+// three steps and in one 2s-aligned run (one direction).
+__global__ void bitonic_global_step3(uint64_t* __restrict__ keys, int64_t n_pad, int64_t size,
+                                     int64_t s) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n_pad / 8) return;
+  const int64_t q = s / 4;
+  const int64_t lo = 8 * q * (t / q) + (t % q);
+  const bool asc = (lo & size) == 0;
+  uint64_t v[8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a) v[a] = keys[lo + a * q];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) cas(v[a], v[a + 4], asc);  // stride s
+  cas(v[0], v[2], asc);  // stride s/2
+  cas(v[1], v[3], asc);
+  cas(v[4], v[6], asc);
+  cas(v[5], v[7], asc);
+#pragma unroll
+  for (int a = 0; a < 8; a += 2) cas(v[a], v[a + 1], asc);  // stride s/4
+#pragma unroll
+  for (int a = 0; a < 8; ++a) keys[lo + a * q] = v[a];
+}
+
 // Register form of the tile kernels: a warp holds 128 consecutive keys of
 // the tile, key j of a thread at tile index warp * 128 + 32 * j + lane.
 // Strides 64 and 32 pair a thread's own keys, strides 16 .. 1 pair lanes
@@ -554,7 +579,11 @@ int sort_keys(uint64_t* keys, int64_t n_pad, cudaStream_t stream) {
     bitonic_tile_sort<<<(unsigned)(n_pad / tile), threads, smem, stream>>>(keys, tile);
   for (int64_t size = (int64_t)tile * 2; size <= n_pad; size <<= 1) {
     for (int64_t stride = size / 2; stride >= tile;) {
-      if (stride / 2 >= tile) {
+      if (stride / 4 >= tile) {
+        bitonic_global_step3<<<blocks_for(n_pad / 8, 256), 256, 0, stream>>>(keys, n_pad, size,
+                                                                              stride);
+        stride >>= 3;
+      } else if (stride / 2 >= tile) {
         bitonic_global_step2<<<blocks_for(n_pad / 4, 256), 256, 0, stream>>>(keys, n_pad, size,
                                                                               stride);
         stride >>= 2;
