@@ -3,19 +3,25 @@
 
 Workload (default ``--workload large-head``): one decode step over 512
 sequences with lengths uniform in [1024, 8192] (multiples of 16), 40 query /
-40 KV heads, head_dim 128, block_size 16 -- about 147K physical blocks,
+40 KV heads, head_dim 128, block_size 16 -- about 155K physical blocks,
 24 GB of INT8 K+V with per-(block, head) fp32 scales from N(0,1) data.  With
 ``--gpus N`` (one process per GPU, launched by torch.distributed.run) the
-sequences are partitioned over ranks by total tokens (strong scaling); each
-rank holds only its sequences' blocks and no collective touches the data
-path.  ``--workload heavy-tail`` runs the 64 x 2048, 8-head decode with 0.1 %
-of K entries x10 instead.
+work is partitioned by ``distributed.plan_decode_shards``: by sequence
+(balanced by tokens), and by KV head where one sequence dominates (strong
+scaling); each rank holds only its shard's blocks and heads and no
+collective touches the data path.  ``--workload heavy-tail`` runs the
+64 x 2048, 8-head decode with 0.1 % of K entries x10 instead, and
+``--workload long-context`` four sequences of 32K-256K tokens at 40 heads
+(the longest holds 53 % of the tokens, so ranks split it by head).
 
-One step = one ``pagedkv_fusion._C.quant_paged_attention`` call (split-K
-decode kernel + combine kernel) over device-resident inputs; K steps are
-timed with CUDA events between barriers and device synchronizations, the
-max over ranks is reported.  The KV working set (24 GB, or 268 MB for the
-heavy-tail workload) is larger than the 126 MB L2, so no flush is needed.
+One step = one ``pagedkv_fusion._C.quant_paged_attention`` call (one
+persistent decode kernel for these shapes) over device-resident inputs; K
+steps are timed with CUDA events between barriers and device
+synchronizations, the max over ranks is reported.  The KV working set
+(24 GB, 268 MB for the heavy-tail workload) is larger than the 126 MB L2, so
+no flush is needed.  After the timed region every rank checks a sample of
+its sequences' outputs against the double-precision C oracle (``parity``);
+the run exits non-zero when that check fails.
 
 Printed JSON (rank 0, one line): ``value`` = decode tokens/s (sequences
 decoded per second, all ranks); ``roofline`` = algorithmic HBM bytes of one
@@ -23,8 +29,11 @@ step / measured step time against the measured copy bandwidth;
 ``e2e`` = the same metric through ``ops.quant_paged_attention`` with q,
 block tables and seq_lens in pinned host memory and the output read back
 every step; ``cpu_baseline`` = the NumPy port of the reference decode on a
-sample of the workload's sequences on this host; ``eviction`` = fused
-score + top-k over 16,384 blocks (k = 2,458) p50 device and wall latency.
+sample of the workload's sequences on this host, scaled to the workload's
+tokens; ``eviction`` = fused score + top-k over 16,384 blocks (k = 2,458)
+p50 device and wall latency; ``extras`` = the heavy-tailed 64 x 2048 decode
+and the reference benchmark's 32/8-head GQA shape, each timed, against the
+roofline and checked against the oracle on every sequence.
 
 ``--impl reference`` times the reference's CPU implementation of the path
 (the NumPy port under oracle/, all host cores) on bounded samples of the
@@ -59,12 +68,17 @@ BLOCK = 16
 HEAD_DIM = 128
 
 WORKLOADS = {
-    "large-head": dict(name="decode_large_head_512seq_L1024-8192_h40_d128_bs16", heads=40),
-    "heavy-tail": dict(name="decode_heavy_tail_64seq_L2048_h8_d128_bs16", heads=8),
+    "large-head": dict(name="decode_large_head_512seq_L1024-8192_h40_d128_bs16", heads=40,
+                       kv_heads=40, parity_seqs=12),
+    "heavy-tail": dict(name="decode_heavy_tail_64seq_L2048_h8_d128_bs16", heads=8, kv_heads=8,
+                       parity_seqs=64),
+    "long-context": dict(name="decode_long_context_4seq_L32K-256K_h40_d128_bs16", heads=40,
+                         kv_heads=40, parity_seqs=2),
     "composition": dict(name="evict15_quantize_decode_1024seq_L4096-32768_h8_d128_bs16_fp16",
                         heads=8),
 }
 EVICT_FRACTION = 0.15
+CPU_MAX_TOKENS = 16384  # longest sequence prefix a CPU-leg process decodes
 
 
 def parse_args():
@@ -77,6 +91,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-eviction", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     return ap.parse_args()
 
 
@@ -85,7 +101,23 @@ def workload_seq_lens(workload: str) -> np.ndarray:
         return problems.large_head_seq_lens(seed=0)
     if workload == "composition":
         return problems.composition_seq_lens(seed=0)
+    if workload == "long-context":
+        return problems.long_context_seq_lens()
     return np.full(64, 2048, dtype=np.int32)
+
+
+def workload_config(wl: dict, lens: np.ndarray) -> dict:
+    """The workload's identity: the same dict on both arms of the bench."""
+    return {"workload": wl["name"], "num_seqs": int(len(lens)),
+            "total_kv_tokens": int(lens.sum()), "heads": wl["heads"],
+            "kv_heads": wl["kv_heads"], "head_dim": HEAD_DIM, "block_size": BLOCK,
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+def cpu_sample(lens: np.ndarray, workers: int) -> np.ndarray:
+    """Sequence indices the CPU legs decode: ``workers`` evenly spaced over
+    the workload (one per process)."""
+    return np.unique(np.linspace(0, len(lens) - 1, min(workers, len(lens))).astype(int))
 
 
 def algorithmic_bytes(lens: np.ndarray, heads: int, kv_heads: int) -> int:
@@ -194,9 +226,10 @@ def run_reference_arm(args):
     wl = WORKLOADS[args.workload]
     lens = workload_seq_lens(args.workload)
     workers = max(1, min(cores_available(), 32))
+    idx = cpu_sample(lens, workers)
     rng = np.random.default_rng(0)
-    tasks = [synthetic_host_sequence(rng, int(lens[i % len(lens)]), wl["heads"],
-                                     args.workload == "heavy-tail") for i in range(workers)]
+    tasks = [synthetic_host_sequence(rng, min(int(lens[i]), CPU_MAX_TOKENS), wl["heads"],
+                                     args.workload == "heavy-tail") for i in idx]
     pool = CpuDecodePool(tasks)
     try:
         for _ in range(args.warmup):
@@ -205,21 +238,33 @@ def run_reference_arm(args):
     finally:
         pool.close()
     t = statistics.fmean(times)
-    value = workers / t
-    sample = (f"{workers} sequences of the workload per step (lengths "
-              f"{sorted(int(x[5]) for x in tasks)[:3]}..., {wl['heads']} heads), one per process")
+    value, sample = cpu_rate(lens, idx, sum(x[5] for x in tasks), t, wl["heads"])
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": len(lens) / value * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl["name"], "parallelism": f"cpu x{workers} processes"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "port",
+        "config": workload_config(wl, lens), "parallelism": f"cpu x{len(idx)} processes",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": len(idx), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def cpu_rate(lens: np.ndarray, idx: np.ndarray, sample_tokens: int, t: float,
+             heads: int) -> tuple[float, str]:
+    """Whole-workload decode tokens/s from a CPU step over the sampled
+    sequences ``idx`` (``sample_tokens`` tokens decoded; sequences longer
+    than CPU_MAX_TOKENS are decoded over their first CPU_MAX_TOKENS) that
+    took ``t`` seconds: the workload's sequences per second at the
+    sample's tokens per second (decode time is linear in tokens)."""
+    step_s = t * float(lens.sum()) / sample_tokens
+    return len(lens) / step_s, (
+        f"{len(idx)} of the {len(lens)} sequences (evenly spaced, {sample_tokens} tokens, "
+        f"{heads} heads), one sequence per single-threaded process, {t:.3f} s per sample "
+        f"step, scaled by the workload's {int(lens.sum())} tokens")
 
 
 # ---------------------------------------------------------------------------
@@ -281,39 +326,6 @@ class ClockSampler:
                 "sm_max_mhz": max(mx) if mx else None,
                 "power_w_max": max(power) if power else None,
                 "samples": len(sm), "reasons": sorted(reasons)}
-
-
-def build_cache(torch, C, lens: np.ndarray, heads: int, heavy: bool, device, seed: int):
-    """Device-resident INT8 paged cache for the given sequences, generated
-    from N(0,1) fp32 chunks and quantized by the native kernel; shuffled
-    block tables as in the reference's generator."""
-    pages = (lens.astype(np.int64) + BLOCK - 1) // BLOCK
-    nb = int(pages.sum())
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    kc = torch.empty((nb, BLOCK, heads, HEAD_DIM), dtype=torch.int8, device=device)
-    vc = torch.empty_like(kc)
-    ks = torch.empty((nb, heads), dtype=torch.float32, device=device)
-    vs = torch.empty_like(ks)
-    chunk = max(1, (1 << 28) // (BLOCK * heads * HEAD_DIM))  # ~1 GB of fp32 per draw
-    for cache, scale, spiky in ((kc, ks, heavy), (vc, vs, False)):
-        for lo in range(0, nb, chunk):
-            hi = min(nb, lo + chunk)
-            x = torch.randn((hi - lo, BLOCK, heads, HEAD_DIM), generator=g, device=device)
-            if spiky:
-                spike = torch.rand(x.shape, generator=g, device=device) < 0.001
-                x = torch.where(spike, x * 10, x)
-            C.quantize_kv_per_block(x, out_q=cache[lo:hi], out_scale=scale[lo:hi])
-            del x
-    rng = np.random.default_rng(seed)
-    perm = rng.permutation(nb).astype(np.int32)
-    width = int(pages.max())
-    bt = np.full((len(lens), width), -1, dtype=np.int32)
-    starts = np.concatenate([[0], np.cumsum(pages)])
-    for s in range(len(lens)):
-        bt[s, :pages[s]] = perm[starts[s]:starts[s + 1]]
-    q = torch.randn((len(lens), heads, HEAD_DIM), generator=g, device=device)
-    return q, kc, ks, vc, vs, bt, nb
 
 
 def eviction_bench(torch, C, ops, iters: int = 200):
@@ -400,6 +412,59 @@ def eviction_bench(torch, C, ops, iters: int = 200):
                 "bytes": stats_bytes}}
 
 
+def read_peak() -> tuple[float, str]:
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        return float(json.loads(pk.read_text())["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs"
+    return 6650.0, "fallback 6650 GB/s"
+
+
+def time_back_to_back(torch, fn, steps: int, warmup: int) -> float:
+    """Mean ms per call of ``fn`` over ``steps`` back-to-back calls between
+    one CUDA-event pair on the current stream (after ``warmup`` calls)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def decode_extra(torch, C, name: str, lens: np.ndarray, heads: int, kv_heads: int, heavy: bool,
+                 device, peak: float, peak_source: str) -> dict:
+    """A further decode configuration on one GPU: timed (200 back-to-back
+    calls), against the roofline, and checked against the oracle on every
+    sequence."""
+    from oracle.parity import sampled_decode_parity
+    q, kc, ks, vc, vs, bt_np, nb = problems.device_paged_cache(lens, kv_heads, heads, device,
+                                                               seed=7, heavy=heavy)
+    bt = torch.from_numpy(bt_np).to(device)
+    sl = torch.from_numpy(lens.astype(np.int32)).to(device)
+    sm = 1.0 / math.sqrt(HEAD_DIM)
+    a = (q, kc, ks, vc, vs, bt, sl, sm)
+    ms = time_back_to_back(torch, lambda: C.quant_paged_attention(*a), 200, 10)
+    out = C.quant_paged_attention(*a)
+    parity = sampled_decode_parity(q, kc, ks, vc, vs, bt_np, lens, sm, out,
+                                   np.arange(len(lens)))
+    byts = algorithmic_bytes(lens, heads, kv_heads)
+    launches = C.quant_paged_attention_kernel_launches(len(lens), heads, kv_heads, HEAD_DIM,
+                                                       BLOCK, bt_np.shape[1])
+    gbs = byts / (ms / 1e3) / 1e9
+    return {"workload": name, "num_seqs": int(len(lens)), "total_kv_tokens": int(lens.sum()),
+            "heads": heads, "kv_heads": kv_heads, "us_per_call": ms * 1e3,
+            "kernel_launches_per_call": launches,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "bytes_per_call": byts,
+                         "basis": "algorithmic bytes / mean CUDA-event time of one call "
+                                  "(200 back-to-back calls)", "peak_source": peak_source},
+            "parity": parity}
+
+
 def run_gpu_arm(args):
     import torch
     import torch.distributed as dist
@@ -415,21 +480,22 @@ def run_gpu_arm(args):
 
     from pagedkv_fusion import _C as C
     from pagedkv_fusion import ops
+    from pagedkv_fusion.distributed import plan_decode_shards
 
     wl = WORKLOADS[args.workload]
-    heads = wl["heads"]
     all_lens = workload_seq_lens(args.workload)
-    shards = problems.balanced_shards(all_lens, world)
-    mine = shards[rank]
-    lens = all_lens[mine]
-    q, kc, ks, vc, vs, bt_np, nb = build_cache(torch, C, lens, heads,
-                                               args.workload == "heavy-tail", device,
-                                               seed=1000 + rank)
+    shards = plan_decode_shards(all_lens, wl["heads"], wl["kv_heads"], world)
+    shard = shards[rank]
+    lens = all_lens[shard.seqs]
+    heads = shard.heads[1] - shard.heads[0]
+    kv_heads = shard.kv_heads
+    q, kc, ks, vc, vs, bt_np, nb = problems.device_paged_cache(
+        lens, kv_heads, heads, device, seed=1000 + rank, heavy=args.workload == "heavy-tail")
     bt = torch.from_numpy(bt_np).to(device)
     sl = torch.from_numpy(lens.astype(np.int32)).to(device)
     sm = 1.0 / math.sqrt(HEAD_DIM)
     step_args = (q, kc, ks, vc, vs, bt, sl, sm)
-    my_bytes = algorithmic_bytes(lens, heads, heads)
+    my_bytes = algorithmic_bytes(lens, heads, kv_heads)
     torch.cuda.synchronize()
 
     def barrier():
@@ -452,9 +518,10 @@ def run_gpu_arm(args):
     # launch duration, inter-launch gaps included.
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    out = None
     t_begin.record(stream)
     for i in range(args.steps):
-        C.quant_paged_attention(*step_args)
+        out = C.quant_paged_attention(*step_args)
     t_end.record(stream)
     barrier()
     clocks = sampler.stop() if sampler else None
@@ -465,6 +532,29 @@ def run_gpu_arm(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_per_step = float(t.item()) / args.steps
     value = len(all_lens) / (ms_per_step / 1e3)
+
+    # parity of the timed step's output on a sample of this rank's sequences
+    # (outside the timed region), reduced over ranks
+    parity = None
+    if not args.no_parity and args.steps > 0:
+        from oracle.parity import sample_sequences, sampled_decode_parity
+        picks = sample_sequences(lens, wl["parity_seqs"])
+        p = sampled_decode_parity(q, kc, ks, vc, vs, bt_np, lens, sm, out, picks)
+        red = torch.tensor([p["max_rel_err"], p["max_abs_err"], 0.0 if p["ok"] else 1.0,
+                            p["sampled_seqs"], p["sampled_tokens"]], dtype=torch.float64,
+                           device=device)
+        if world > 1:
+            mx = red[:3].clone()
+            sm_ = red[3:].clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            dist.all_reduce(sm_, op=dist.ReduceOp.SUM)
+            red = torch.cat([mx, sm_])
+        r = red.cpu().tolist()
+        parity = {"ok": r[2] == 0.0, "max_rel_err": r[0], "max_abs_err": r[1],
+                  "sampled_seqs": int(r[3]), "sampled_tokens": int(r[4]),
+                  "tolerance": "max rel err 1e-3 and allclose(rtol=2e-4, atol=2e-4)",
+                  "oracle": "double-precision C restatement of paged_attention_ref on the "
+                            "sampled sequences' pages copied from the timed cache"}
 
     # end-to-end: host (pinned) q / tables / lengths in, host output back
     e2e = None
@@ -501,27 +591,23 @@ def run_gpu_arm(args):
                      else "heavy-tail ncu capture's traffic/algorithmic ratio x this "
                           "workload's algorithmic bytes")
     launches_per_step = C.quant_paged_attention_kernel_launches(
-        len(lens), heads, heads, HEAD_DIM, BLOCK, bt_np.shape[1])
+        len(lens), heads, kv_heads, HEAD_DIM, BLOCK, bt_np.shape[1])
     plan_name = ("persistent decode_stream_kernel" if launches_per_step == 1
                  else "split-K decode kernel + combine")
+    peak, peak_source = read_peak()
     result = None
     if rank == 0:
-        peaks = {}
-        pk = ROOT / "MEASURED_PEAKS.json"
-        if pk.exists():
-            peaks = json.loads(pk.read_text())
-        peak = float(peaks.get("hbm_gbs", 6650.0))
         achieved = my_bytes / (mean_launch_ms / 1e3) / 1e9
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "s8/f32", "data": "synthetic",
-            "config": {"workload": wl["name"], "num_seqs": int(len(all_lens)),
-                       "total_kv_tokens": int(all_lens.sum()), "heads": heads,
-                       "kv_heads": heads, "head_dim": HEAD_DIM, "block_size": BLOCK,
-                       "blocks_rank0": nb, "parallelism": f"sequence-sharded x{world}",
-                       "l2": "inputs larger than L2 (no flush)"},
+            "config": workload_config(wl, all_lens),
+            "parallelism": (f"{world // shard.head_split} sequence group(s) x "
+                            f"{shard.head_split} KV-head slice(s)"),
+            "rank0": {"seqs": int(len(lens)), "kv_heads": kv_heads, "blocks": nb,
+                      "kv_tokens": int(lens.sum())},
             "kv_tokens_per_s": float(all_lens.sum()) / (ms_per_step / 1e3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -530,38 +616,53 @@ def run_gpu_arm(args):
                                   "CUDA-event time of one quant_paged_attention call over the "
                                   "timed region (events around the back-to-back calls, "
                                   f"{launches_per_step} kernel launch(es) per call: {plan_name})",
-                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if pk.exists()
-                         else "fallback 6650 GB/s"},
-            "clocks": clocks, "e2e": e2e,
+                         "peak_source": peak_source},
+            "parity": parity, "clocks": clocks, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
         }
-    # CPU baseline and the eviction latency on rank 0 at N = 1
+    # CPU baseline, eviction latency and the extra decode shapes on rank 0 at N = 1
     if rank == 0 and world == 1:
         if not args.no_eviction:
             result["eviction"] = eviction_bench(torch, C, ops)
         if not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline_from_device(
                 torch, args, lens, step_args, bt_np, heads)
+        if not args.no_extras:
+            del step_args, q, kc, ks, vc, vs, out
+            torch.cuda.empty_cache()
+            result["extras"] = {
+                "heavy_tail": decode_extra(torch, C, WORKLOADS["heavy-tail"]["name"],
+                                           workload_seq_lens("heavy-tail"), 8, 8, True, device,
+                                           peak, peak_source),
+                "gqa_32_8": decode_extra(torch, C, "decode_gqa_64seq_L2048_h32_kv8_d128_bs16",
+                                         np.full(64, 2048, dtype=np.int32), 32, 8, False, device,
+                                         peak, peak_source),
+            }
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if result is not None:
         print(json.dumps(result), flush=True)
-    return 0
+    ok = parity is None or parity["ok"]
+    if result is not None and "extras" in result:
+        ok = ok and all(x["parity"]["ok"] for x in result["extras"].values())
+    return 0 if ok else 1
 
 
 def cpu_baseline_from_device(torch, args, lens, step_args, bt_np, heads):
     """The NumPy port of the reference decode on a sample of this run's own
-    sequences (their pages copied to the host), one process per core."""
+    sequences (their pages copied to the host), one process per core, scaled
+    to the workload's tokens."""
     q, kc, ks, vc, vs, _, _, _ = step_args
     workers = max(1, min(cores_available(), 32))
-    idx = np.linspace(0, len(lens) - 1, workers).astype(int)
+    idx = cpu_sample(lens, workers)
     tasks = []
     for s in idx:
-        pages = bt_np[s, :(int(lens[s]) + BLOCK - 1) // BLOCK].astype(np.int64)
+        L = min(int(lens[s]), CPU_MAX_TOKENS)
+        pages = bt_np[s, :(L + BLOCK - 1) // BLOCK].astype(np.int64)
         p = torch.from_numpy(pages).to(kc.device)
         tasks.append((q[s].cpu().numpy(), kc[p].cpu().numpy(), ks[p].cpu().numpy(),
-                      vc[p].cpu().numpy(), vs[p].cpu().numpy(), int(lens[s])))
+                      vc[p].cpu().numpy(), vs[p].cpu().numpy(), L))
     pool = CpuDecodePool(tasks)
     try:
         pool.step()
@@ -569,10 +670,9 @@ def cpu_baseline_from_device(torch, args, lens, step_args, bt_np, heads):
     finally:
         pool.close()
     t = statistics.median(times)
-    return {"value": len(tasks) / t, "unit": UNIT, "cores": workers, "kind": "port",
-            "sample": f"{len(tasks)} of the {len(lens)} sequences ({int(lens[idx].sum())} "
-                      f"tokens, {heads} heads), one sequence per single-threaded process, "
-                      f"median of 5 steps of {t:.2f} s"}
+    value, sample = cpu_rate(lens, idx, sum(x[5] for x in tasks), t, heads)
+    return {"value": value, "unit": UNIT, "cores": len(idx), "kind": "port",
+            "sample": sample + ", median of 5 steps"}
 
 
 # ---------------------------------------------------------------------------

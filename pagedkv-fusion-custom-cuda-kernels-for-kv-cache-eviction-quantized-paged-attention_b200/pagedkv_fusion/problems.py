@@ -14,10 +14,16 @@ The ``workload_*`` helpers build the named benchmark workloads:
                            entries x10 before quantization
 * decode large-head     -- 512 seqs, L ~ U[1024, 8192] (multiple of 16),
                            40/40 heads, ~147K blocks (~24 GB INT8 KV)
+* decode long-context    -- 4 seqs of 256K / 128K / 64K / 32K tokens, 40/40
+                           heads (the longest holds over half of the
+                           tokens: no split by sequence balances ranks)
 * evict -> quantize -> decode composition -- 1,024 seqs, L ~ U[4096, 32768]
                            (multiple of 16), 8/8 heads, fp16 K/V, 15 % of
                            the blocks evicted (``composition_seq_lens``;
                            ``composition_problem`` builds small instances)
+
+``device_paged_cache`` builds any of the decode workloads' INT8 caches
+directly on a CUDA device (N(0,1) data quantized by the native kernel).
 """
 
 from __future__ import annotations
@@ -32,9 +38,11 @@ __all__ = [
     "eviction_problem",
     "decode_heavy_tail_problem",
     "large_head_seq_lens",
+    "long_context_seq_lens",
     "composition_seq_lens",
     "composition_problem",
     "balanced_shards",
+    "device_paged_cache",
 ]
 
 
@@ -135,6 +143,13 @@ def large_head_seq_lens(seed: int = 0, num_seqs: int = 512, lo: int = 1024,
     return np.clip(lens, lo, hi).astype(np.int32)
 
 
+def long_context_seq_lens() -> np.ndarray:
+    """Four long sequences of 262,144 / 131,072 / 65,536 / 32,768 tokens.
+    The longest is 53 % of all tokens, so sharding by sequence alone cannot
+    give ranks equal work beyond one GPU."""
+    return np.array([262144, 131072, 65536, 32768], dtype=np.int32)
+
+
 def composition_seq_lens(seed: int = 0, num_seqs: int = 1024, lo: int = 4096,
                          hi: int = 32768, block_size: int = 16) -> np.ndarray:
     """Sequence lengths uniform in [lo, hi], rounded to multiples of 16."""
@@ -189,3 +204,48 @@ def balanced_shards(seq_lens, world_size: int) -> list[np.ndarray]:
         shards[r].append(i)
         loads[r] += int(lens[i])
     return [np.array(sorted(s), dtype=np.int64) for s in shards]
+
+
+def device_paged_cache(seq_lens, kv_heads: int, num_heads: int, device, seed: int,
+                       heavy: bool = False, block_size: int = 16, head_dim: int = 128):
+    """An INT8 paged cache for ``seq_lens`` built on a CUDA device.
+
+    K and V are drawn N(0,1) in fp32 chunks of about 1 GB (K entries x10
+    with probability 0.001 when ``heavy``, the heavy-tail recipe) and
+    quantized per (block, head) by the native kernel straight into the
+    cache; the block order is a seeded random permutation, as in the
+    reference's generator.  Returns ``(q, k_cache, k_scale, v_cache,
+    v_scale, block_tables, num_blocks)`` with ``q`` ``[S, num_heads, D]``
+    on the device and ``block_tables`` a host int32 array ``[S, max pages]``
+    (-1 padded).
+    """
+    import torch
+
+    from . import _C
+    lens = np.asarray(seq_lens, dtype=np.int64)
+    pages = (lens + block_size - 1) // block_size
+    nb = int(pages.sum())
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    kc = torch.empty((nb, block_size, kv_heads, head_dim), dtype=torch.int8, device=device)
+    vc = torch.empty_like(kc)
+    ks = torch.empty((nb, kv_heads), dtype=torch.float32, device=device)
+    vs = torch.empty_like(ks)
+    chunk = max(1, (1 << 28) // (block_size * kv_heads * head_dim))
+    for cache, scale, spiky in ((kc, ks, heavy), (vc, vs, False)):
+        for lo in range(0, nb, chunk):
+            hi = min(nb, lo + chunk)
+            x = torch.randn((hi - lo, block_size, kv_heads, head_dim), generator=g, device=device)
+            if spiky:
+                spike = torch.rand(x.shape, generator=g, device=device) < 0.001
+                x = torch.where(spike, x * 10, x)
+            _C.quantize_kv_per_block(x, out_q=cache[lo:hi], out_scale=scale[lo:hi])
+            del x
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(nb).astype(np.int32)
+    bt = np.full((len(lens), max(1, int(pages.max()) if len(lens) else 1)), -1, dtype=np.int32)
+    starts = np.concatenate([[0], np.cumsum(pages)])
+    for s in range(len(lens)):
+        bt[s, :pages[s]] = perm[starts[s]:starts[s + 1]]
+    q = torch.randn((len(lens), num_heads, head_dim), generator=g, device=device)
+    return q, kc, ks, vc, vs, bt, nb

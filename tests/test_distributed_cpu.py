@@ -125,3 +125,92 @@ def test_decode_partition_is_balanced_and_complete():
         np.testing.assert_array_equal(allidx, np.arange(lens.size))
         loads = [int(lens[s].sum()) for s in shards]
         assert max(loads) - min(loads) <= int(lens.max())
+
+
+def _coverage(shards, S, Hkv):
+    """(sequence, kv head) -> how many ranks hold it."""
+    cnt = np.zeros((S, Hkv), dtype=np.int64)
+    for sh in shards:
+        for s in sh.seqs:
+            cnt[s, sh.kv_lo:sh.kv_hi] += 1
+    return cnt
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_decode_plan_by_sequence_when_sequences_balance(world):
+    """The 512-sequence large-head batch stays sequence-sharded: every
+    (sequence, KV head) on exactly one rank, ranks within 2 % of even."""
+    from pagedkv_fusion import problems
+    from pagedkv_fusion.distributed import plan_decode_shards
+    lens = problems.large_head_seq_lens(0)
+    shards = plan_decode_shards(lens, 40, 40, world)
+    assert len(shards) == world
+    assert all(sh.head_split == 1 and (sh.kv_lo, sh.kv_hi) == (0, 40) for sh in shards)
+    assert (_coverage(shards, lens.size, 40) == 1).all()
+    loads = [sh.tokens(lens) * sh.kv_heads for sh in shards]
+    assert max(loads) <= 1.02 * sum(loads) / world
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_decode_plan_splits_heads_when_one_sequence_dominates(world):
+    """Four sequences of which one holds 53 % of the tokens: sequence
+    sharding alone would leave one rank with over half the work, so the
+    ranks split the KV heads (40 / world each) and every rank does exactly
+    1 / world of the work."""
+    from pagedkv_fusion import problems
+    from pagedkv_fusion.distributed import plan_decode_shards
+    lens = problems.long_context_seq_lens()
+    shards = plan_decode_shards(lens, 40, 40, world)
+    assert shards[0].head_split == world
+    assert (_coverage(shards, lens.size, 40) == 1).all()
+    loads = {sh.tokens(lens) * sh.kv_heads for sh in shards}
+    assert loads == {int(lens.sum()) * 40 // world}
+    # GQA: query heads follow their KV heads
+    gq = plan_decode_shards(lens, 32, 8, world)
+    for sh in gq:
+        assert sh.heads == (sh.kv_lo * 4, sh.kv_hi * 4)
+
+
+def test_decode_plan_mixed_split_and_uneven_heads():
+    """A dominant sequence with KV heads that do not divide by the world
+    size: the planner uses the largest head split that divides both (here 2
+    of 4 ranks per sequence group) and still covers every (sequence, head)
+    once."""
+    from pagedkv_fusion.distributed import plan_decode_shards
+    lens = np.array([9000, 3000, 2000, 1000, 500], dtype=np.int32)
+    shards = plan_decode_shards(lens, 6, 6, 4)
+    assert shards[0].head_split == 2
+    assert (_coverage(shards, lens.size, 6) == 1).all()
+    with pytest.raises(ValueError):
+        plan_decode_shards(lens, 6, 4, 2)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_head_and_sequence_shards_reassemble_the_decode(world):
+    """Cutting a global cache into the planner's shards, decoding each shard
+    with the oracle and stitching the outputs gives the global decode."""
+    import torch
+    from oracle import oracle as O
+    from pagedkv_fusion import problems
+    from pagedkv_fusion.distributed import (gather_decode_outputs, local_decode_inputs,
+                                            plan_decode_shards)
+    rng = np.random.default_rng(world)
+    q, k, v, bt, sl, sm = problems.make_paged_kv_problem(rng, 5, 16, 8, 64, 16, 300)
+    big = int(np.argmax((bt >= 0).sum(axis=1)))
+    sl[:] = np.minimum(sl, 40)
+    sl[big] = int((bt[big] >= 0).sum()) * 16  # one long sequence dominates
+    kq, ks = O.quantize_kv_per_block(k)
+    vq, vs = O.quantize_kv_per_block(v)
+    want = O.paged_attention(q, kq, ks, vq, vs, bt, sl, sm)
+    shards = plan_decode_shards(sl, 16, 8, world)
+    assert shards[0].head_split > 1
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    outs = []
+    for sh in shards:
+        lq, lk, lks, lv, lvs, lbt, lsl = local_decode_inputs(sh, T(q), T(kq), T(ks), T(vq),
+                                                             T(vs), T(bt), T(sl))
+        assert lk.shape[2] == sh.kv_heads and lq.shape[1] == sh.kv_heads * 2
+        outs.append(T(O.paged_attention(lq.numpy(), lk.numpy(), lks.numpy(), lv.numpy(),
+                                        lvs.numpy(), lbt.numpy(), lsl.numpy(), sm)))
+    got = gather_decode_outputs(shards, outs, 5, 16).numpy()
+    np.testing.assert_allclose(got, want, rtol=1e-6, atol=1e-6)

@@ -1,5 +1,6 @@
 """Two ranks on two GPUs (NCCL): the sharded eviction exchange with the real
-kernels, and sequence-sharded decode, against the oracle.
+kernels, sequence-sharded decode, and head-sharded decode of a batch in
+which one sequence dominates, against the oracle.
 
 Needs two visible GPUs; skips otherwise (the single-GPU suite covers the
 kernels, tests/test_distributed_cpu.py the exchange logic on gloo)."""
@@ -34,7 +35,8 @@ def _worker(rank, world, port, q):
         import torch.distributed as dist
         from oracle import oracle as O
         from pagedkv_fusion import _C, problems
-        from pagedkv_fusion.distributed import (shard_block_range, shard_sequences,
+        from pagedkv_fusion.distributed import (local_decode_inputs, plan_decode_shards,
+                                                shard_block_range, shard_sequences,
                                                 sharded_eviction_select)
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
@@ -61,9 +63,26 @@ def _worker(rank, world, port, q):
         got = _C.quant_paged_attention(*d, sm).cpu().numpy()
         want_d = O.paged_attention(qf[mine], kq, ks, vq, vs, bt[mine], sl[mine], sm)
         err = float(np.abs(got - want_d).max() / max(np.abs(want_d).max(), 1e-30))
+        # decode split by KV head: one long sequence dominates the batch
+        rng = np.random.default_rng(8)
+        qf, kf, vf, bt, sl, sm = problems.make_paged_kv_problem(rng, 4, 16, 8, 128, 16, 700)
+        big = int(np.argmax((bt >= 0).sum(axis=1)))
+        sl[:] = np.minimum(sl, 48)
+        sl[big] = int((bt[big] >= 0).sum()) * 16
+        kq, ks = O.quantize_kv_per_block(kf)
+        vq, vs = O.quantize_kv_per_block(vf)
+        shards = plan_decode_shards(sl, 16, 8, world)
+        sh = shards[rank]
+        T = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        local = local_decode_inputs(sh, T(qf), T(kq), T(ks), T(vq), T(vs), T(bt), T(sl))
+        got_h = _C.quant_paged_attention(*local, sm).cpu().numpy()
+        h0, h1 = sh.heads
+        want_h = O.paged_attention(qf, kq, ks, vq, vs, bt, sl, sm)[sh.seqs][:, h0:h1]
+        err_h = float(np.abs(got_h - want_h).max() / max(np.abs(want_h).max(), 1e-30))
+        head_ok = sh.head_split == world and sh.kv_heads == 8 // world
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, ev_ok, err))
+        q.put((rank, ev_ok and head_ok, max(err, err_h)))
     except Exception:
         q.put((rank, "crash", traceback.format_exc()))
 

@@ -4,12 +4,24 @@ pkv_quant_paged_attention_noalloc serves callers that cannot allocate
 device memory (a plugin given only input/output pointers by a framework
 that owns all device memory, or a serving path that must not pay
 cudaMalloc's synchronization): its split-K scratch is a fixed array inside
-the library.  This test calls it twice in a row on the same inputs, with no
-workspace, and checks both outputs against the allocating entry point's
-(same kernels, so equal within the attention tolerance used everywhere:
-rtol/atol 2e-4).  It also checks that a call too large for the scratch is
-rejected.  The file sorts last so a stop-at-first-failure run has already
-run every other test; it also passes alone in a fresh process.
+the library, shared by every call on a device and never cleared.
+
+Both kernel families that keep state in that array are exercised, each on
+two problems of different shapes called back to back, so every call starts
+on the scratch contents the previous one left:
+
+* groups of 2 and 4 query heads per KV head take the tensor-core kernel,
+  whose split partials are merged by a second kernel;
+* one query head per KV head takes the persistent stream kernel (one
+  launch per call, asserted), whose launch-tagged arrival counters live in
+  the scratch and are not reset between calls.
+
+Each output is compared bit for bit with the allocating entry point (same
+plan, same kernels, deterministic merges) and with the double-precision C
+oracle within the attention tolerance used everywhere (rtol/atol 2e-4, max
+relative error 1e-3).  A call too large for the scratch is rejected.  The
+file sorts last so a stop-at-first-failure run has already run every other
+test; it also passes alone in a fresh process.
 """
 
 from __future__ import annotations
@@ -22,10 +34,14 @@ import pytest
 import torch
 
 from conftest import ensure_native_built
+from oracle import c_oracle
 from oracle import oracle as O
 from pagedkv_fusion import problems
 
 pytestmark = pytest.mark.gpu
+
+ATTN_RTOL = ATTN_ATOL = 2e-4
+ATTN_MAXREL = 1e-3
 
 
 def _lib():
@@ -36,6 +52,9 @@ def _lib():
     f.restype = ct.c_int
     lib.pkv_noalloc_scratch_bytes.restype = ct.c_size_t
     lib.pkv_last_error_string.restype = ct.c_char_p
+    n = lib.pkv_quant_paged_attention_kernel_launches
+    n.argtypes = [ct.c_int32] * 6
+    n.restype = ct.c_int
     return lib
 
 
@@ -50,31 +69,52 @@ def _call_noalloc(lib, q, kq, ks, vq, vs, bt, sl, sm):
     return rc, out
 
 
-def _device_problem(seed, S, H, Hkv, L):
+def _problem(seed, S, H, Hkv, L):
     q, k, v, bt, sl, sm = problems.make_paged_kv_problem(np.random.default_rng(seed), S, H, Hkv,
                                                          128, 16, L)
     kq, ks = O.quantize_kv_per_block(k)
     vq, vs = O.quantize_kv_per_block(v)
-    d = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (q, kq, ks, vq, vs, bt, sl)]
-    return d, sm
+    host = (q, kq, ks, vq, vs, bt, sl)
+    d = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in host]
+    return host, d, sm
 
 
-def test_noalloc_matches_allocating_entry_point_twice():
-    if not torch.cuda.is_available():
-        pytest.fail("gpu test run without a visible CUDA device")
-    lib = _lib()
+def _check_twice(lib, cases, launches):
     from pagedkv_fusion import _C
-    # two different problems, so the second call must overwrite the first's
-    # partials in the shared scratch
-    for seed, (S, H, Hkv, L) in ((1, (12, 16, 8, 3000)), (2, (5, 32, 8, 1700))):
-        d, sm = _device_problem(seed, S, H, Hkv, L)
-        want = _C.quant_paged_attention(*d, sm)
+    for seed, (S, H, Hkv, L) in cases:
+        host, d, sm = _problem(seed, S, H, Hkv, L)
+        assert lib.pkv_quant_paged_attention_kernel_launches(
+            S, H, Hkv, 128, 16, host[5].shape[1]) == launches
+        want = _C.quant_paged_attention(*d, sm).cpu().numpy()
+        ref = c_oracle.paged_attention(*host, sm)
+        np.testing.assert_allclose(want, ref, rtol=ATTN_RTOL, atol=ATTN_ATOL)
         for _ in range(2):
             rc, got = _call_noalloc(lib, *d, sm)
             assert rc == 0, lib.pkv_last_error_string().decode()
             torch.cuda.synchronize()
-            np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=2e-4,
-                                       atol=2e-4)
+            got = got.cpu().numpy()
+            np.testing.assert_array_equal(got, want)
+            np.testing.assert_allclose(got, ref, rtol=ATTN_RTOL, atol=ATTN_ATOL)
+            assert float(np.abs(got - ref).max()) / float(np.abs(ref).max()) <= ATTN_MAXREL
+
+
+def test_noalloc_tensor_core_path_twice():
+    """Groups of 2 and 4 (tensor-core kernel + combine): the second problem
+    overwrites the first's partials in the shared scratch."""
+    if not torch.cuda.is_available():
+        pytest.fail("gpu test run without a visible CUDA device")
+    _check_twice(_lib(), ((1, (12, 16, 8, 3000)), (2, (5, 32, 8, 1700))), launches=2)
+
+
+def test_noalloc_stream_kernel_reuses_its_counters():
+    """One query head per KV head (persistent stream kernel, one launch):
+    the first problem has 37 x 8 units, the second 5 x 4, so the second
+    call's units map to arrival counters the first call left behind, and
+    each problem has units split over several CTAs (counters in use)."""
+    if not torch.cuda.is_available():
+        pytest.fail("gpu test run without a visible CUDA device")
+    _check_twice(_lib(), ((3, (37, 8, 8, 1000)), (4, (5, 4, 4, 9000)), (3, (37, 8, 8, 1000))),
+                 launches=1)
 
 
 def test_noalloc_rejects_work_beyond_its_scratch():
