@@ -824,34 +824,35 @@ __device__ __forceinline__ void merge_partials(const float* __restrict__ ws_acc,
   den = warp_sum(den);
 }
 
-// Arrival counters need no reset before a launch.  A counter holds
-// (launch tag << kArrivalBits) | arrivals.  At kernel start the CTA that owns
-// the first page of a split unit stamps the unit's counter with this
-// launch's tag and a count of 0 (stamp_unit); the unit's CTAs then arrive
-// with one atomic add each, and the arrival that completes the set writes 0
-// back, so a CUDA-graph replay of the same launch (same tag) finds no stale
-// tag either.  An arrival that finds another tag came before the stamp (its
-// CTA finished before the unit's first CTA started): the stamp overwrites
-// its add, so it waits for the stamp (bounded) and adds again.  Returns 1
-// for the completing arrival, 0 otherwise, -1 when the stamp never came.
+// Arrival counters need no reset before a launch, and no CTA waits for
+// another to prepare them.  A counter holds (launch tag << kArrivalBits) |
+// arrivals.  Each arrival is one compare-and-swap (acquire-release, GPU
+// scope): a counter that carries this launch's tag gets one more arrival; a
+// counter with any other tag -- 0 after a completed set, or what an earlier
+// launch or another process left -- is replaced by (tag, 1).  The arrival
+// that completes the set writes 0 back, so a CUDA-graph replay of the same
+// launch (same tag) starts from 0 as well.  The first guess is 0, the state
+// a completed set leaves, so a unit's first arrival usually takes one
+// atomic and the others two.  Returns 1 for the completing arrival, 0
+// otherwise, -1 if the swap kept failing (another kernel racing on the
+// same workspace).
 constexpr int kArrivalBits = 20;
-__device__ __forceinline__ void stamp_unit(unsigned long long* ctr, unsigned long long tag) {
-  *reinterpret_cast<volatile unsigned long long*>(ctr) = tag << kArrivalBits;
-}
 __device__ __forceinline__ int arrive_on_unit(unsigned long long* ctr, unsigned long long tag,
                                               int nseg) {
   constexpr unsigned long long kCount = (1ull << kArrivalBits) - 1;
-  for (;;) {
-    const unsigned long long old = atomic_add_acq_rel_gpu_u64(ctr, 1ull);
-    if ((old >> kArrivalBits) == tag) {
-      const bool last = (int)(old & kCount) + 1 == nseg;
+  const unsigned long long fresh = (tag << kArrivalBits) | 1ull;
+  unsigned long long expect = 0ull;
+  for (int tries = 0; tries < (1 << 20); ++tries) {
+    const unsigned long long want = (expect >> kArrivalBits) == tag ? expect + 1ull : fresh;
+    const unsigned long long seen = atomic_cas_acq_rel_gpu(ctr, expect, want);
+    if (seen == expect) {
+      const bool last = (int)(want & kCount) == nseg;
       if (last) *reinterpret_cast<volatile unsigned long long*>(ctr) = 0ull;
       return last ? 1 : 0;
     }
-    const uint64_t t0 = global_timer_ns();
-    while ((*reinterpret_cast<volatile unsigned long long*>(ctr) >> kArrivalBits) != tag)
-      if (global_timer_ns() - t0 > 2000000000ull) return -1;
+    expect = seen;
   }
+  return -1;
 }
 
 template <int BS, int HG, int G>
@@ -1073,21 +1074,6 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
       const uint64_t policy = l2_policy_evict_first();
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      {  // while the first table loads: stamp the counters of the split units
-         // whose first page is here
-        StreamIter w = it;
-        StreamChunk c;
-        const int me = blockIdx.x;
-        while (w.next(c)) {
-          if (!c.seg_first || c.whole) continue;
-          int first, last;
-          unit_owners(s_pseq, c.s, c.g, ng, unit_cost, P, n_ctas, first, last);
-          const int u = c.s * ng + c.g;
-          if (me == first) stamp_unit(&unit_arrivals[u], launch_tag);
-          if (last - first + 1 > kMergeGroup && (me - first) % kMergeGroup == 0)
-            stamp_unit(&unit_arrivals[S * ng + u + me], launch_tag);  // its group's counter
-        }
-      }
       int ns = 0;
       for (int i = 0; it.next(ch); ++i) {
         const int b = i & 1;

@@ -13,6 +13,14 @@ as they are).  Keep the workload small (a few GB on the device) when using
     python -m pagedkv_fusion.profile_kernels attention --num-seqs 64 --seq-len 2048
     python -m pagedkv_fusion.profile_kernels quantize --blocks 60000 --ncu --out prof_q
     python -m pagedkv_fusion.profile_kernels eviction --num-blocks 16384
+    python -m pagedkv_fusion.profile_kernels eviction --num-blocks 1200000 --ncu \
+        --kernel regex:bitonic_global --per-call 12
+
+Above 16,384 blocks the eviction call runs the multi-kernel selection
+(radix prefilter, tile sorts, global merge passes) instead of the one-launch
+cluster kernel; ``--ncu`` then needs ``--kernel`` (the kernel to capture)
+and ``--per-call`` (how many launches matching it one call makes, so the
+capture skips the warm-up calls' launches).
 """
 
 from __future__ import annotations
@@ -26,7 +34,7 @@ import sys
 
 # kernel-name pattern and launches per call of each target's calls
 KERNELS = {
-    "eviction": ("regex:evict", 1),
+    "eviction": ("regex:evict_cluster", 1),  # the one-launch path (<= 16,384 blocks)
     "attention": ("regex:decode_(stream|tc_stream|tc|fast|generic)_kernel", 1),
     "quantize": ("regex:quantize_bulk", 1),
 }
@@ -109,21 +117,45 @@ def main(argv=None) -> int:
     ap.add_argument("--ncu", action="store_true",
                     help="run once plainly, then capture one launch under ncu")
     ap.add_argument("--out", default="prof", help="ncu report path (without .ncu-rep)")
+    ap.add_argument("--kernel", default=None,
+                    help="ncu -k pattern overriding the target's (e.g. regex:bitonic_global)")
+    ap.add_argument("--per-call", type=int, default=None,
+                    help="launches matching --kernel per call (default: the target's)")
     args = ap.parse_args(argv)
+    if args.ncu and args.target == "eviction" and args.num_blocks > 16384 and args.kernel is None:
+        ap.error("above 16,384 blocks eviction runs the multi-kernel selection: pass --kernel "
+                 "(and --per-call) to name the kernel to capture")
     if not args.ncu:
         run_workload(args)
         return 0
     ncu = shutil.which("ncu")
     if ncu is None:
         sys.exit("ERROR: ncu not found on PATH")
-    plain = [sys.executable, "-m", "pagedkv_fusion.profile_kernels"] + [
-        a for a in (argv if argv is not None else sys.argv[1:]) if a != "--ncu"]
+    raw = list(argv if argv is not None else sys.argv[1:])
+    plain = [sys.executable, "-m", "pagedkv_fusion.profile_kernels"]
+    skip = False
+    for a in raw:  # the plain run takes the workload arguments only
+        if skip:
+            skip = False
+            continue
+        if a == "--ncu":
+            continue
+        if a in ("--kernel", "--per-call", "--out"):
+            skip = True
+            continue
+        if a.startswith(("--kernel=", "--per-call=", "--out=")):
+            continue
+        plain.append(a)
     env = dict(os.environ)
     rc = subprocess.run(plain, env=env).returncode
     if rc != 0:
         print(f"plain run exited {rc}: not profiled", file=sys.stderr)
         return rc
     pattern, per_call = KERNELS[args.target]
+    if args.kernel is not None:
+        pattern = args.kernel
+    if args.per_call is not None:
+        per_call = args.per_call
     cmd = [ncu, "--set", "full", "--clock-control", "none", "-k", pattern,
            "-s", str(args.warmup * per_call), "-c", "1", "-o", args.out, "--force-overwrite"] + plain
     print("running:", " ".join(cmd), flush=True)
