@@ -528,7 +528,18 @@ def run_gpu_arm(args):
     total_ms = t_begin.elapsed_time(t_end)
     mean_launch_ms = total_ms / args.steps
     t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+    per_rank = None
     if world > 1:
+        # every rank's step time and share, for the imbalance of the plan
+        mine = torch.tensor([total_ms / args.steps, float(lens.sum()), float(len(lens)),
+                             float(kv_heads)], dtype=torch.float64, device=device)
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+        rows = [g.cpu().tolist() for g in gathered]
+        ms = [r[0] for r in rows]
+        per_rank = {"ms_per_step": ms, "kv_tokens": [int(r[1]) for r in rows],
+                    "seqs": [int(r[2]) for r in rows], "kv_heads": [int(r[3]) for r in rows],
+                    "max_over_mean_ms": max(ms) / (sum(ms) / len(ms))}
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_per_step = float(t.item()) / args.steps
     value = len(all_lens) / (ms_per_step / 1e3)
@@ -608,6 +619,7 @@ def run_gpu_arm(args):
                             f"{shard.head_split} KV-head slice(s)"),
             "rank0": {"seqs": int(len(lens)), "kv_heads": kv_heads, "blocks": nb,
                       "kv_tokens": int(lens.sum())},
+            "ranks": per_rank,
             "kv_tokens_per_s": float(all_lens.sum()) / (ms_per_step / 1e3),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
