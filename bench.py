@@ -386,9 +386,10 @@ def eviction_bench(torch, C, ops, iters: int = 200):
     st_us = []
     for _ in range(50):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        torch.cuda._sleep(100_000)  # the events bracket device execution, not the enqueue
+        e0.record(stream)
         C.attention_stats(kpool, qh, 1 / math.sqrt(128))
-        e1.record()
+        e1.record(stream)
         e1.synchronize()
         st_us.append(e0.elapsed_time(e1) * 1e3)
     stats_bytes = kpool.numel() * 2 + 16384 * 16 * 8 * 4 * 2 + 16384 * 16 * 4

@@ -10,6 +10,11 @@ with a static CUDA runtime, and the library is written to
 pagedkv_fusion/lib/libpagedkv_sm100.so, where pagedkv_fusion._C loads it.
 The library needs no CUDA driver at load time (driver entry points are
 resolved lazily), so it loads on GPU-less build machines too.
+
+csrc/pkv_pycall.c (direct CPython calls into the C ABI for the eviction
+latency path) is compiled with the host C compiler against this
+interpreter's headers into pagedkv_fusion/lib/_pkv_pycall<ext suffix>,
+linked to the library beside it.
 """
 
 from __future__ import annotations
@@ -66,6 +71,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     with ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: _compile(s, force, verbose), srcs))
     if not force and LIB.exists() and LIB.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
+        _build_pycall()
         return LIB
     tmp = LIB.with_suffix(f".{os.getpid()}.tmp")
     cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs)]
@@ -74,7 +80,32 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         sys.stderr.write(res.stdout + res.stderr)
         raise RuntimeError("nvcc link failed")
     os.replace(tmp, LIB)
+    _build_pycall(force=True)
     return LIB
+
+
+def pycall_path() -> Path:
+    import sysconfig
+    return LIB_DIR / ("_pkv_pycall" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def _build_pycall(force: bool = False) -> Path:
+    import sysconfig
+    src = CSRC / "pkv_pycall.c"
+    out = pycall_path()
+    deps = [src, LIB, INCLUDE / "pagedkv_fusion.h"]
+    if not force and out.exists() and out.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return out
+    tmp = out.with_suffix(f".{os.getpid()}.tmp")
+    cmd = [os.environ.get("CC", "gcc"), "-O2", "-shared", "-fPIC", "-std=c11",
+           "-I", sysconfig.get_paths()["include"], "-I", str(INCLUDE), str(src), "-o", str(tmp),
+           "-L", str(LIB_DIR), "-lpagedkv_sm100", "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("compiling pkv_pycall.c failed")
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":

@@ -618,7 +618,6 @@ __global__ void __launch_bounds__(kFastThreads, 2)
 // pages per CTA of the grid) is spread over fewer CTAs.
 
 constexpr int kStreamMaxSeqs = 1024;
-constexpr int kMergeDepth = 2;  // partial rows in flight per merging warp
 constexpr int kStreamThreads = kConsumers + 64;  // + TMA warp + table warp
 constexpr int kTmaWarp = kConsumerWarps;
 constexpr int kTableWarp = kConsumerWarps + 1;
@@ -781,7 +780,12 @@ constexpr int kMergeGroup = 16;
 // Merges n partial rows (acc relative to exp2(m), with (m, l)) of one query
 // head, row j at slot slot_of(j): a = sum_j w_j acc_j and den = sum_j w_j l_j
 // with w_j = exp2(m_j - M), M = max_j m_j; rows with m = -inf add nothing.
-// Rows are added in index order (deterministic), kMergeDepth in flight.
+// Rows are added in index order (deterministic).  The merge runs on the
+// kernel's critical path after the GPU-wide stream of page loads, where
+// every L2 round trip is long: the (m, l) of the first 32 rows and the
+// first kMergeBatch acc rows are requested together, so a merge of up to
+// kMergeBatch partials costs one round trip.
+constexpr int kMergeBatch = 8;
 template <typename SlotFn>
 __device__ __forceinline__ void merge_partials(const float* __restrict__ ws_acc,
                                                const float2* __restrict__ ws_ml, int n, int lane,
@@ -789,7 +793,15 @@ __device__ __forceinline__ void merge_partials(const float* __restrict__ ws_acc,
   auto load_ml = [&](int j) {
     return j < n ? __ldcg(&ws_ml[slot_of(j)]) : make_float2(-INFINITY, 0.0f);
   };
+  auto load_rows = [&](int j0, float4 (&x)[kMergeBatch]) {
+#pragma unroll
+    for (int jj = 0; jj < kMergeBatch; ++jj)
+      x[jj] = __ldcg(reinterpret_cast<const float4*>(ws_acc + slot_of(min(j0 + jj, n - 1)) * 128) +
+                     lane);
+  };
+  float4 x[kMergeBatch];
   const float2 ml0 = load_ml(lane);  // the first 32 are kept for the second pass
+  load_rows(0, x);
   M = ml0.x;
   for (int b = 32; b < n; b += 32) M = fmaxf(M, load_ml(b + lane).x);
   M = warp_max(M);
@@ -803,14 +815,10 @@ __device__ __forceinline__ void merge_partials(const float* __restrict__ ws_acc,
       den += w * ml.y;
     }
     const int nb = min(32, n - b);
-    for (int j0 = 0; j0 < nb; j0 += kMergeDepth) {
-      float4 x[kMergeDepth];
+    for (int j0 = 0; j0 < nb; j0 += kMergeBatch) {
+      if (b + j0 > 0) load_rows(b + j0, x);
 #pragma unroll
-      for (int jj = 0; jj < kMergeDepth; ++jj)
-        x[jj] = __ldcg(reinterpret_cast<const float4*>(ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * 128) +
-                       lane);
-#pragma unroll
-      for (int jj = 0; jj < kMergeDepth; ++jj) {
+      for (int jj = 0; jj < kMergeBatch; ++jj) {
         const float wj = __shfl_sync(0xffffffffu, w, (j0 + jj) & 31);
         if (j0 + jj < nb && wj != 0.0f) {
           a.x += wj * x[jj].x;
@@ -831,17 +839,18 @@ __device__ __forceinline__ void merge_partials(const float* __restrict__ ws_acc,
 // counter with any other tag -- 0 after a completed set, or what an earlier
 // launch or another process left -- is replaced by (tag, 1).  The arrival
 // that completes the set writes 0 back, so a CUDA-graph replay of the same
-// launch (same tag) starts from 0 as well.  The first guess is 0, the state
-// a completed set leaves, so a unit's first arrival usually takes one
-// atomic and the others two.  Returns 1 for the completing arrival, 0
-// otherwise, -1 if the swap kept failing (another kernel racing on the
-// same workspace).
+// launch (same tag) starts from 0 as well.  The first guess is the value
+// the caller read (relaxed) while it computed its last chunk, so an arrival
+// usually takes one atomic: the last arrival of a unit is on the kernel's
+// critical path, and each failed guess costs another L2 round trip.
+// Returns 1 for the completing arrival, 0 otherwise, -1 if the swap kept
+// failing (another kernel racing on the same workspace).
 constexpr int kArrivalBits = 20;
 __device__ __forceinline__ int arrive_on_unit(unsigned long long* ctr, unsigned long long tag,
-                                              int nseg) {
+                                              int nseg, unsigned long long guess) {
   constexpr unsigned long long kCount = (1ull << kArrivalBits) - 1;
   const unsigned long long fresh = (tag << kArrivalBits) | 1ull;
-  unsigned long long expect = 0ull;
+  unsigned long long expect = guess;
   for (int tries = 0; tries < (1 << 20); ++tries) {
     const unsigned long long want = (expect >> kArrivalBits) == tag ? expect + 1ull : fresh;
     const unsigned long long seen = atomic_cas_acq_rel_gpu(ctr, expect, want);
@@ -1126,7 +1135,25 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
   for (int g = 0; g < F::kGPW; ++g) acc_run[g][0] = acc_run[g][1] = acc_run[g][2] = acc_run[g][3] = 0.0f;
   bool live = true;
   int ns = 0, cur_s = -1, cur_g = -1;
+  // the first-level arrival of a split unit: its counter and count
+  auto arrival_of = [&](const StreamChunk& c, int& first, int& last, int& nseg, int& ngroups,
+                        int& g_lo, int& g_hi) -> unsigned long long* {
+    unit_owners(s_pseq, c.s, c.g, ng, unit_cost, P, n_ctas, first, last);
+    nseg = last - first + 1;
+    ngroups = (nseg + kMergeGroup - 1) / kMergeGroup;
+    g_lo = first + (int)(blockIdx.x - first) / kMergeGroup * kMergeGroup;
+    g_hi = min(last, g_lo + kMergeGroup - 1);
+    const int u = c.s * ng + c.g;
+    return ngroups == 1 ? &unit_arrivals[u] : &unit_arrivals[S * ng + u + g_lo];
+  };
   for (int i = 0; it.next(ch); ++i) {
+    // a split unit's last chunk in this CTA: read its arrival counter now,
+    // so the arrival after the chunk usually swaps on the first try
+    unsigned long long arrival_guess = 0ull;
+    if (tid == 0 && ch.seg_last && !ch.whole) {
+      int f, l, n, ngr, glo, ghi;
+      arrival_guess = ld_relaxed_gpu_u64(arrival_of(ch, f, l, n, ngr, glo, ghi));
+    }
     const uint8_t* meta = smem + C::kOffMeta + (i & 1) * C::kMetaBytes;
     const int* m_phys = reinterpret_cast<const int*>(meta + C::kMetaPhys);
     const float* m_ks = reinterpret_cast<const float*>(meta + C::kMetaKs);
@@ -1399,21 +1426,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
         }
         // the unit's CTAs [first, last] in page order: every one owns pages
         // (n_ctas <= P gives each CTA at least one position)
-        int first, last;
-        unit_owners(s_pseq, ch.s, ch.g, ng, unit_cost, P, n_ctas, first, last);
-        const int nseg = last - first + 1;
-        const int ngroups = (nseg + kMergeGroup - 1) / kMergeGroup;
-        const int g_lo = first + (int)(blockIdx.x - first) / kMergeGroup * kMergeGroup;
-        const int g_hi = min(last, g_lo + kMergeGroup - 1);
-        const int n_units = S * ng;
+        int first, last, nseg, ngroups, g_lo, g_hi;
+        unsigned long long* ctr = arrival_of(ch, first, last, nseg, ngroups, g_lo, g_hi);
         // every partial store of this CTA is ordered before thread 0's
         // release by the barrier; the last arrival acquires all of them
         named_barrier(1, kConsumers);
         if (tid == 0) {
-          const int r = ngroups == 1
-                            ? arrive_on_unit(&unit_arrivals[u], launch_tag, nseg)
-                            : arrive_on_unit(&unit_arrivals[n_units + u + g_lo], launch_tag,
-                                             g_hi - g_lo + 1);
+          const int r = arrive_on_unit(ctr, launch_tag, ngroups == 1 ? nseg : g_hi - g_lo + 1,
+                                       arrival_guess);
           if (r < 0) record_error(err, kDevWaitTimeout);
           s_tmp[32] = r == 1;
         }
@@ -1448,7 +1468,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
           if (final_pass) break;
           named_barrier(1, kConsumers);  // the group's partial is stored
           if (tid == 0) {
-            const int r = arrive_on_unit(&unit_arrivals[u], launch_tag, ngroups);
+            const int r = arrive_on_unit(&unit_arrivals[u], launch_tag, ngroups, 0ull);
             if (r < 0) record_error(err, kDevWaitTimeout);
             s_tmp[33] = r == 1;
           }

@@ -78,6 +78,13 @@ __device__ __forceinline__ unsigned long long atomic_cas_acq_rel_gpu(unsigned lo
   return old;
 }
 
+// 64-bit relaxed load at GPU scope (a hint: no ordering with other accesses).
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

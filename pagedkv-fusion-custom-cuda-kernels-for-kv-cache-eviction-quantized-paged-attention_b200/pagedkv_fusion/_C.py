@@ -15,7 +15,6 @@ this module fails with ``ImportError`` when that library has not been built.
 from __future__ import annotations
 
 import ctypes as ct
-import os
 from pathlib import Path
 
 import torch
@@ -24,6 +23,26 @@ _LIB_PATH = Path(__file__).resolve().parent / "lib" / "libpagedkv_sm100.so"
 if not _LIB_PATH.exists():
     raise ImportError(f"{_LIB_PATH} is not built (run build.py in the package root)")
 _lib = ct.CDLL(str(_LIB_PATH))
+
+
+def _load_pycall():
+    """The METH_FASTCALL module over the same library (csrc/pkv_pycall.c):
+    the eviction calls' arguments cost ~0.2 us there against ~2.2 us as
+    ctypes conversions, on a path whose GPU time is ~13 us."""
+    import importlib.machinery
+    import importlib.util
+    import sysconfig
+    path = _LIB_PATH.parent / ("_pkv_pycall" + sysconfig.get_config_var("EXT_SUFFIX"))
+    if not path.exists():
+        raise ImportError(f"{path} is not built (run build.py in the package root)")
+    loader = importlib.machinery.ExtensionFileLoader("_pkv_pycall", str(path))
+    spec = importlib.util.spec_from_file_location("_pkv_pycall", str(path), loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
+_fast = _load_pycall()
 
 _P, _I32, _I64, _F, _SZ = ct.c_void_p, ct.c_int32, ct.c_int64, ct.c_float, ct.c_size_t
 
@@ -66,8 +85,13 @@ LIBRARY_PATH = str(_LIB_PATH)
 _DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 
-_FUSED_WS_CACHE: dict = {}  # (num_blocks, k, device, env) -> workspace bytes
+# Workspace bytes per (num_blocks, k, device).  The size depends on the
+# selection path, which PKV_EVICTION_MULTI_KERNEL can change between calls;
+# a call that finds its cached size too small (PKV_ERR_WORKSPACE) asks the
+# library again and retries once, so the environment is not read per call.
+_FUSED_WS_CACHE: dict = {}
 _SELECT_WS_CACHE: dict = {}
+_ERR_WORKSPACE = 3
 
 
 def _check(rc: int):
@@ -136,9 +160,10 @@ def eviction_scores(recency, frequency, attn_weights, valid_mask, w_recency=0.4,
     att = attn_weights if attn_weights.is_contiguous() else attn_weights.contiguous()
     msk = valid_mask if valid_mask.is_contiguous() else valid_mask.contiguous()
     out = torch.empty(nb, dtype=_F32, device=rec.device)
-    rc = _scores(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
-                 out.data_ptr(), nb, bs, w_recency, w_frequency, w_attention,
-                 torch._C._cuda_getCurrentRawStream(rec.device.index))
+    rc = _fast.eviction_scores(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
+                               out.data_ptr(), nb, bs, float(w_recency), float(w_frequency),
+                               float(w_attention),
+                               torch._C._cuda_getCurrentRawStream(rec.device.index))
     if rc:
         _check(rc)
     return out
@@ -308,13 +333,19 @@ def eviction_select(scores, k: int):
     out = torch.empty(kk, dtype=torch.int64, device=s.device)
     if kk == 0:
         return out
-    key = (n, kk, s.device.index, os.environ.get("PKV_EVICTION_MULTI_KERNEL"))
+    dev = s.device.index
+    key = (n, kk, dev)
     nbytes = _SELECT_WS_CACHE.get(key)
     if nbytes is None:
         nbytes = _SELECT_WS_CACHE[key] = _select_ws(n, kk)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=s.device) if nbytes else None
-    rc = _select(s.data_ptr(), n, kk, out.data_ptr(), 0 if ws is None else ws.data_ptr(),
-                 nbytes, torch._C._cuda_getCurrentRawStream(s.device.index))
+    stream = torch._C._cuda_getCurrentRawStream(dev)
+    for attempt in (0, 1):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=s.device) if nbytes else None
+        rc = _fast.eviction_select(s.data_ptr(), n, kk, out.data_ptr(),
+                                   None if ws is None else ws.data_ptr(), nbytes, stream)
+        if rc != _ERR_WORKSPACE or attempt:
+            break
+        nbytes = _SELECT_WS_CACHE[key] = _select_ws(n, kk)
     if rc:
         _check(rc)
     return out
@@ -324,10 +355,10 @@ def eviction_scores_select(recency, frequency, attn_weights, valid_mask, k: int,
                            w_recency=0.4, w_frequency=0.3, w_attention=0.3):
     """Scores and the k selected block ids from one call: ``(scores, idx)``.
 
-    Checks are plain attribute tests and the workspace size is cached per
-    (num_blocks, k, device, forced multi-kernel path): this call sits on the
-    eviction latency path, where a few microseconds of Python are a large
-    share of the total.
+    Checks are plain attribute tests, the workspace size is cached per
+    (num_blocks, k, device) and the call goes through the METH_FASTCALL
+    module: this call sits on the eviction latency path, where a few
+    microseconds of host time are a large share of the total.
     """
     if not (recency.is_cuda and frequency.is_cuda and attn_weights.is_cuda
             and valid_mask.is_cuda):
@@ -352,16 +383,20 @@ def eviction_scores_select(recency, frequency, attn_weights, valid_mask, k: int,
     scores = torch.empty(nb, dtype=_F32, device=dev)
     kk = k if k < nb else nb
     idx = torch.empty(kk, dtype=torch.int64, device=dev)
-    key = (nb, kk, dev.index, os.environ.get("PKV_EVICTION_MULTI_KERNEL"))
+    key = (nb, kk, dev.index)
     nbytes = _FUSED_WS_CACHE.get(key)
     if nbytes is None:
-        nbytes = _fused_ws(nb, kk) if kk else 0
-        _FUSED_WS_CACHE[key] = nbytes
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
-    rc = _fused(rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(),
-                scores.data_ptr(), nb, bs, w_recency, w_frequency, w_attention, kk,
-                idx.data_ptr(), None if ws is None else ws.data_ptr(), nbytes,
-                torch._C._cuda_getCurrentRawStream(dev.index))
+        nbytes = _FUSED_WS_CACHE[key] = _fused_ws(nb, kk) if kk else 0
+    stream = torch._C._cuda_getCurrentRawStream(dev.index)
+    for attempt in (0, 1):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
+        rc = _fast.eviction_scores_select(
+            rec.data_ptr(), freq.data_ptr(), att.data_ptr(), msk.data_ptr(), scores.data_ptr(), nb,
+            bs, float(w_recency), float(w_frequency), float(w_attention), kk, idx.data_ptr(),
+            None if ws is None else ws.data_ptr(), nbytes, stream)
+        if rc != _ERR_WORKSPACE or attempt:
+            break
+        nbytes = _FUSED_WS_CACHE[key] = _fused_ws(nb, kk) if kk else 0
     if rc:
         _check(rc)
     return scores, idx

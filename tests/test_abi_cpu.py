@@ -181,3 +181,19 @@ def test_ops_fails_loudly_without_a_device():
     with pytest.raises(RuntimeError, match="CUDA device"):
         ops.eviction_scores(np.zeros(2, np.float32), np.zeros(2, np.float32),
                             np.zeros((2, 16), np.float32), np.ones((2, 16), bool))
+
+
+def test_fastcall_module_reaches_the_same_library():
+    """The METH_FASTCALL module the eviction calls use: built beside the
+    library, argument count checked, and the library's own status codes
+    returned (invalid sizes are rejected before any CUDA call)."""
+    ensure_native_built()
+    from pagedkv_fusion import _C
+    fast = _C._fast
+    with pytest.raises(TypeError):
+        fast.eviction_select(None, 4, 2)
+    assert fast.eviction_select(None, 4, -1, None, None, 0, None) == 1
+    assert fast.eviction_scores(None, None, None, None, None, -1, 16, 0.4, 0.3, 0.3, None) == 1
+    assert fast.eviction_scores_select(None, None, None, None, None, 8, 16, 0.4, 0.3, 0.3, -2,
+                                       None, None, 0, None) == 1
+    assert "k" in _C._last_error().decode()

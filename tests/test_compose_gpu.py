@@ -194,11 +194,18 @@ def test_report_sections(cuda, tmp_path):
         assert {"num_seqs", "seq_len", "int8_kernel_p50_ms", "fp16_sdpa_gathered_p50_ms"} <= set(row)
 
 
-@pytest.mark.parametrize("dtype,bs,heads", [(torch.float16, 16, 8), (torch.float32, 16, 3),
-                                            (torch.bfloat16, 32, 8), (torch.float16, 32, 40)])
-def test_attention_stats_match_oracle(cuda, dtype, bs, heads):
+@pytest.mark.parametrize("dtype,bs,heads,warp_path", [
+    # bulk-streamed path (blocks <= 32 KB, KV heads dividing 8)
+    (torch.float16, 16, 8, False), (torch.float32, 16, 4, False), (torch.bfloat16, 16, 2, False),
+    (torch.float16, 32, 4, False), (torch.float16, 16, 1, False),
+    # one warp per (block, head) from global memory: other shapes, or forced
+    (torch.float16, 16, 8, True), (torch.float32, 16, 3, False), (torch.bfloat16, 32, 8, False),
+    (torch.float16, 32, 40, False)])
+def test_attention_stats_match_oracle(cuda, monkeypatch, dtype, bs, heads, warp_path):
     """Key-derived attention statistics (the eviction score's attention
     input) against the float64 restatement; then fed to the fused scorer."""
+    if warp_path:
+        monkeypatch.setenv("PKV_ATTN_STATS_WARP", "1")
     rng = np.random.default_rng(heads + bs)
     nb = 777
     k = torch.from_numpy(rng.standard_normal((nb, bs, heads, 128), dtype=np.float32)).to(dtype)
