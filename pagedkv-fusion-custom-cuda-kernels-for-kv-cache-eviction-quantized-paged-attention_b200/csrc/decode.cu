@@ -2253,43 +2253,58 @@ __global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
       ++k;
     }
   } else if (warp == 0) {
-    // ---- TMA: per unit its K tiles, then its V tiles ---------------------------
+    // ---- TMA: per unit its K tiles, then its V tiles.  The whole warp
+    // issues: lane 0 waits for a stage and arms its barrier, then lane i
+    // issues page i of the tile (one 2 KB box per page and KV head; one
+    // issuing thread managed ~one box per 85 ns).
+    const uint64_t policy = l2_policy_evict_first();
     if (lane == 0) {
-      const uint64_t policy = l2_policy_evict_first();
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      TcsUnit un;
-      int k = 0, ns = 0;
-      bool ok_run = true;
-      for (int64_t u = blockIdx.x; u < n_units && ok_run; u += stride) {
-        if (!tcs_unit(u, num_kv_heads, max_splits, pages_per_split, seq_lens, max_blocks_per_seq, un))
-          continue;
-        const int b = k & 1;
-        if (!mbar_wait_bounded(&meta_full[b], (uint32_t)(k >> 1) & 1u, err)) {
-          record_error(err, kDevWaitTimeout);
-          break;
-        }
-        const int* phys_t = reinterpret_cast<const int*>(meta(b) + C::kMetaPhys);
-        for (int kind = 0; kind < 2 && ok_run; ++kind) {
-          for (int ti = 0; ti < un.n_tiles; ++ti, ++ns) {
-            const int st = ns % C::kStages;
+    }
+    TcsUnit un;
+    int k = 0, ns = 0;
+    bool ok_run = true;
+    for (int64_t u = blockIdx.x; u < n_units && ok_run; u += stride) {
+      if (!tcs_unit(u, num_kv_heads, max_splits, pages_per_split, seq_lens, max_blocks_per_seq, un))
+        continue;
+      const int b = k & 1;
+      bool ok = true;
+      if (lane == 0 && !mbar_wait_bounded(&meta_full[b], (uint32_t)(k >> 1) & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        ok = false;
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int* phys_t = reinterpret_cast<const int*>(meta(b) + C::kMetaPhys);
+      for (int kind = 0; kind < 2 && ok_run; ++kind) {
+        for (int ti = 0; ti < un.n_tiles; ++ti, ++ns) {
+          const int st = ns % C::kStages;
+          const int pb = ti * 8, pe = min(un.np, pb + 8);
+          bool oks = true;
+          if (lane == 0) {
             if (!mbar_wait_bounded(&empty[st], ((uint32_t)(ns / C::kStages) & 1u) ^ 1u, err)) {
               record_error(err, kDevWaitTimeout);
-              ok_run = false;
-              break;
+              oks = false;
+            } else {
+              mbar_arrive_expect_tx(&full[st], (uint32_t)((pe - pb) * BS * 128));
             }
-            const int pb = ti * 8, pe = min(un.np, pb + 8);
-            mbar_arrive_expect_tx(&full[st], (uint32_t)((pe - pb) * BS * 128));
-            for (int pg = pb; pg < pe; ++pg)
-              tma_load_3d(smem + st * kStageBytes + (pg - pb) * BS * 128, kind ? &map_v : &map_k,
-                          &full[st], 0, un.j, max(phys_t[pg], 0) * BS, policy);
           }
+          oks = __shfl_sync(0xffffffffu, oks, 0);
+          __syncwarp();  // the stage is armed before any of its copies is issued
+          if (!oks) {
+            ok_run = false;
+            break;
+          }
+          if (lane < pe - pb)
+            tma_load_3d(smem + st * kStageBytes + lane * BS * 128, kind ? &map_v : &map_k,
+                        &full[st], 0, un.j, max(phys_t[pb + lane], 0) * BS, policy);
         }
-        mbar_arrive(&meta_free[b]);
-        ++k;
       }
-      drain_ring(full, C::kStages, ns);  // no copy outlives the CTA
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_free[b]);
+      ++k;
     }
+    if (lane == 0) drain_ring(full, C::kStages, ns);  // no copy outlives the CTA
   } else if (warp == 1) {
     // ---- MMA issue ---------------------------------------------------------
     if (lane == 0) {

@@ -1,7 +1,8 @@
 """Profiling workloads for the kernels, and an Nsight Compute wrapper.
 
 The counterpart of the reference's ``scripts/profile_kernels.py`` (targets
-``eviction`` and ``attention``, the same defaults), plus ``quantize``.
+``eviction`` and ``attention``, the same defaults), plus ``quantize`` and
+``stats`` (attention statistics from an fp16 key pool).
 Without ``--ncu`` it only runs the workload: a few warm-up calls, then the
 calls to profile.  With ``--ncu`` it first runs the same workload without
 the profiler and, only if that exits cleanly, once more under ``ncu`` with a
@@ -13,6 +14,7 @@ as they are).  Keep the workload small (a few GB on the device) when using
     python -m pagedkv_fusion.profile_kernels attention --num-seqs 64 --seq-len 2048
     python -m pagedkv_fusion.profile_kernels quantize --blocks 60000 --ncu --out prof_q
     python -m pagedkv_fusion.profile_kernels eviction --num-blocks 16384
+    python -m pagedkv_fusion.profile_kernels stats --blocks 16384 --kv-heads 8 --ncu --out prof_s
     python -m pagedkv_fusion.profile_kernels eviction --num-blocks 1200000 --ncu \
         --kernel regex:bitonic_global --per-call 12
 
@@ -37,6 +39,7 @@ KERNELS = {
     "eviction": ("regex:evict_cluster", 1),  # the one-launch path (<= 16,384 blocks)
     "attention": ("regex:decode_(stream|tc_stream|tc|fast|generic)_kernel", 1),
     "quantize": ("regex:quantize_bulk", 1),
+    "stats": ("regex:attn_logits", 1),
 }
 
 
@@ -87,12 +90,21 @@ def _quantize(args, torch):
     return lambda: _C.quantize_kv_per_block_except(x, skip, q, s)
 
 
+def _stats(args, torch):
+    from pagedkv_fusion import _C
+    g = torch.Generator(device="cuda").manual_seed(5)
+    nb, Hkv = args.blocks, args.kv_heads
+    k = torch.randn((nb, args.block_size, Hkv, 128), device="cuda", generator=g).half()
+    q = torch.randn((Hkv, 128), device="cuda", generator=g)
+    return lambda: _C.attention_stats(k, q, 1 / math.sqrt(128))
+
+
 def run_workload(args) -> None:
     import torch
     if not torch.cuda.is_available():
         sys.exit("ERROR: no CUDA device visible")
-    call = {"eviction": _eviction, "attention": _attention, "quantize": _quantize}[args.target](
-        args, torch)
+    call = {"eviction": _eviction, "attention": _attention, "quantize": _quantize,
+            "stats": _stats}[args.target](args, torch)
     for _ in range(args.warmup):
         call()
     torch.cuda.synchronize()
@@ -110,7 +122,8 @@ def main(argv=None) -> int:
     ap.add_argument("--seq-len", type=int, default=2048, help="attention: tokens per sequence")
     ap.add_argument("--heads", type=int, default=32, help="attention: query heads")
     ap.add_argument("--kv-heads", type=int, default=8, help="attention / quantize: KV heads")
-    ap.add_argument("--blocks", type=int, default=60000, help="quantize: fp16 blocks")
+    ap.add_argument("--blocks", type=int, default=60000,
+                    help="quantize / stats: fp16 blocks")
     ap.add_argument("--skip-fraction", type=float, default=0.15, help="quantize: blocks skipped")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=3)

@@ -123,11 +123,11 @@ def test_attention_stats_definition_properties():
 
 def test_profile_driver_targets_and_no_device():
     """The profiling driver (counterpart of the reference's
-    scripts/profile_kernels.py) knows the three targets and refuses to run
+    scripts/profile_kernels.py) knows its four targets and refuses to run
     without a device instead of falling back to anything."""
     import torch
     from pagedkv_fusion import profile_kernels as pk
-    assert sorted(pk.KERNELS) == ["attention", "eviction", "quantize"]
+    assert sorted(pk.KERNELS) == ["attention", "eviction", "quantize", "stats"]
     if torch.cuda.is_available():
         pytest.skip("a device is visible")
     with pytest.raises(SystemExit):

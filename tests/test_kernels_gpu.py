@@ -342,6 +342,13 @@ def test_attention_stream_one_sequence_over_all_ctas(cuda):
         assert torch.equal(o, outs[0])
 
 
+def _tc_form(monkeypatch, form):
+    """persistent: three CTAs per SM walking the units (the default);
+    split: one CTA per split."""
+    if form == "split":
+        monkeypatch.setenv("PKV_DECODE_TC_SPLIT", "1")
+
+
 @pytest.mark.parametrize("form", ["persistent", "split"])
 @pytest.mark.parametrize("group", [2, 4, 8])
 @pytest.mark.parametrize("pages", ["auto", "8", "16", "32"])
@@ -353,8 +360,7 @@ def test_attention_tensor_core_gqa(cuda, monkeypatch, form, group, pages):
     split), both followed by the combine kernel."""
     if pages != "auto":
         monkeypatch.setenv("PKV_DECODE_SPLIT_PAGES", pages)
-    if form == "split":
-        monkeypatch.setenv("PKV_DECODE_TC_SPLIT", "1")
+    _tc_form(monkeypatch, form)
     from pagedkv_fusion import _C
     for seed, S, hkv, L in ((31, 7, 4, 1500), (32, 3, 2, 130), (33, 12, 8, 700), (34, 2, 1, 17)):
         assert _C.quant_paged_attention_kernel_launches(S, group * hkv, hkv, 128, 16, 94) == 2
@@ -393,6 +399,24 @@ def test_tensor_core_persistent_merge_edges(cuda, group):
     assert rc == 0
     assert torch.equal(out, got)
     assert cuda.read_device_error(reset=True) == 0
+
+
+@pytest.mark.parametrize("group", [2, 4, 8])
+def test_tensor_core_forms_agree_bitwise(cuda, monkeypatch, group):
+    """The persistent and split forms run the same arithmetic per unit (same
+    MMAs, same epilogue): bit-identical outputs, on a batch that gives every
+    persistent CTA several units."""
+    prob = problems.make_paged_kv_problem(np.random.default_rng(90 + group), 40, group * 8, 8,
+                                          128, 16, 2000)
+    args = quantized_problem(*prob)
+    want = c_oracle.paged_attention(*args)
+    outs = {}
+    for form in ("persistent", "split"):
+        with monkeypatch.context() as mp:
+            _tc_form(mp, form)
+            outs[form] = run_attention(args)
+    assert_attention_close(outs["persistent"], want)
+    assert torch.equal(outs["persistent"], outs["split"])
 
 
 def test_attention_tensor_core_matches_cuda_core_path(cuda, monkeypatch):
