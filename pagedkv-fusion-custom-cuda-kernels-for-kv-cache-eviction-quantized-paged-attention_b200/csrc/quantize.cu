@@ -50,33 +50,61 @@ __device__ __noinline__ uint32_t quantize_word_exact(float x0, float x1, float x
          ((uint32_t)(quantize_one(x3, scale) & 255) << 24);
 }
 
+// Two fp32 lanes in one 64-bit register, for Blackwell's packed f32x2
+// arithmetic (each lane rounded exactly like the scalar instruction).
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // Four codes packed little-endian.  Fast path, for a head whose absmax is
 // finite and whose scale has a finite reciprocal rcp = 1/scale (rounded to
 // nearest): y = x * rcp differs from fl(x/scale) by at most
 // 1.5 * 2^-23 * |x/scale| <= 2^-15.5, because |x| <= absmax keeps
-// |x/scale| <= 127 * (1 + 2^-24).  Adding 1.5 * 2^23 rounds y to an integer
-// half-to-even and leaves it, two's complement, in the low mantissa bits;
-// y minus that integer is exact.  When every y lies farther than 2^-15 from
-// a half-integer, fl(x/scale) rounds to the same integers; otherwise (about
-// 2.4e-4 of words) the exact division decides.  |y| < 127.5, so the clamp
-// to [-127, 127] never binds.  Heads with a non-finite absmax, or a scale
-// below 2^-128 (reciprocal overflows), take the exact division.
+// |x/scale| <= 127 * (1 + 2^-24).  With d = 2^-15 and K = 1.5 * 2^23:
+// y - d and y + d are exact (|y| < 128, whose ulp is at most 2^-17), and
+// adding K rounds each to an integer half-to-even, left two's complement in
+// the low mantissa bits.  If both round to the same integer, no half-integer
+// lies in [y - d, y + d], so every value within 2^-15.5 of y -- fl(x/scale)
+// among them -- rounds to that integer too, and it is the code.  Otherwise
+// (about 2.4e-4 of words) the exact division decides.  |y| < 127.5, so the
+// clamp to [-127, 127] never binds.  Heads with a non-finite absmax, or a
+// scale below 2^-128 (reciprocal overflows), take the exact division.  The
+// arithmetic runs two values per instruction (f32x2), which matters: the
+// bulk quantizer is bound by instruction issue, not by HBM.
 __device__ __forceinline__ uint32_t quantize_word(const float (&f)[4], float scale, float rcp,
                                                   bool fast) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
   if (fast) {
-    uint32_t b[4];
-    bool near = false;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float y = __fmul_rn(f[i], rcp);
-      const float z = __fadd_rn(y, kRound);
-      near |= fabsf(__fsub_rn(y, __fsub_rn(z, kRound))) >= 0.5f - 0x1p-15f;
-      b[i] = __float_as_uint(z);
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    constexpr float kWin = 0x1p-15f;
+    const uint64_t r2 = f32x2(rcp, rcp), k2 = f32x2(kRound, kRound), w2 = f32x2(kWin, kWin);
+    const uint64_t y01 = mul_f32x2(f32x2(f[0], f[1]), r2);
+    const uint64_t y23 = mul_f32x2(f32x2(f[2], f[3]), r2);
+    const uint64_t hi01 = add_f32x2(add_f32x2(y01, w2), k2);
+    const uint64_t lo01 = add_f32x2(sub_f32x2(y01, w2), k2);
+    const uint64_t hi23 = add_f32x2(add_f32x2(y23, w2), k2);
+    const uint64_t lo23 = add_f32x2(sub_f32x2(y23, w2), k2);
+    if (((hi01 ^ lo01) | (hi23 ^ lo23)) == 0ull) {
+      const uint32_t b0 = (uint32_t)hi01, b1 = (uint32_t)(hi01 >> 32);
+      const uint32_t b2 = (uint32_t)hi23, b3 = (uint32_t)(hi23 >> 32);
+      return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
     }
-    if (!near)
-      return __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040),
-                         0x5410);
   }
   return quantize_word_exact(f[0], f[1], f[2], f[3], scale);
 }
