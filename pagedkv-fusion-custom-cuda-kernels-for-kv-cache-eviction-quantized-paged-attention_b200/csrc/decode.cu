@@ -87,6 +87,21 @@ bool make_cache_map(CUtensorMap* map, const int8_t* cache, int64_t num_blocks, i
   return r == CUDA_SUCCESS;
 }
 
+// 4-D view (d, token, head, block) of the cache [NB, 16, hkv, 128] int8: a
+// page box (128, 16, hkv, 1) lands as [head][token][128 B].
+bool make_page_map(CUtensorMap* map, const int8_t* cache, int64_t num_blocks, int hkv) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[4] = {128, 16, (cuuint64_t)hkv, (cuuint64_t)num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)hkv * 128, 128, (cuuint64_t)16 * hkv * 128};
+  cuuint32_t box[4] = {128, 16, (cuuint32_t)hkv, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(cache), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Small cache of encoded maps: a serving loop calls decode with the same
 // cache tensors every step.
 struct MapKey {
@@ -111,7 +126,8 @@ bool cached_cache_map(CUtensorMap* out, const int8_t* cache, int64_t nb, int bs,
       *out = maps[i];
       return true;
     }
-  if (!make_cache_map(out, cache, nb, bs, hkv, hg)) return false;
+  if (!(hg < 0 ? make_page_map(out, cache, nb, hkv) : make_cache_map(out, cache, nb, bs, hkv, hg)))
+    return false;
   keys[next] = key;
   maps[next] = *out;
   next = (next + 1) % 16;
@@ -2494,6 +2510,761 @@ __global__ void __launch_bounds__(256, TcsCfg<G>::kMinBlocks)
 }
 
 // ===========================================================================
+// Tensor-core decode over whole pages (GQA groups of 2/4/8, bs 16, D 128)
+// ===========================================================================
+//
+// The per-head tensor-core kernels above copy one 2 KB box per (page, KV
+// head): on the paged layout such a stream needs ~200 KB in flight per SM to
+// reach the HBM peak (a TMA-only probe: 5.1 TB/s at one CTA per SM with a
+// 10-stage ring, against 6.3 TB/s for whole 16 KB pages).  This kernel copies
+// whole pages, one box per page, through a 4-D tensor map ordered (D, token,
+// head, block), so a page lands as [head][token][128 B]: a 128-row stage
+// holds 8 / Hkv pages, row r = (page, head, token) with head = (r / 16) % Hkv.
+//
+//   q.K  D1[128 rows][NQ] = stage (K-major, 128 rows x 128 B) x Qd^T, where
+//        Qd holds the 3 digit planes of every (KV head h, query head g):
+//        column n = 3 (h G + g) + plane.  Row r only needs the 3G columns of
+//        its own head; the rest of the product is discarded (the tensor pipe
+//        has the room: ~30 % busy at the HBM rate).
+//   p.V  D2[128 dims][NQ] += stage^T (MN-major) x P^T, where P is
+//        block-diagonal: P[n][r] is the probability plane n of row r if the
+//        head of column n is the head of row r, else 0.
+//
+// Scheduling is the MHA stream kernel's: one unit per sequence (all KV
+// heads), the units' pages flattened into one virtual range split evenly
+// over the CTAs (one per SM), chunks of at most 256 tokens, a running
+// (m, l, acc) per query head across the chunks of a unit, partials and
+// arrival counters where a unit straddles CTAs.  Roles: warp 0 issues the
+// page copies, warp 1 the MMAs, warps 2-3 fill the chunk tables (block ids
+// and scales; query digits), warps 4-7 (one per TMEM lane quarter) turn
+// logits into probability tiles and read the results.
+template <int HKV, int G>
+struct TcpCfg {
+  static constexpr int kHeads = HKV * G;  // query heads of a unit
+  // columns per KV head (its G query heads x 3 digit planes, padded so that
+  // a warp's two heads start on a 16-column boundary of tensor memory)
+  static constexpr int kCS = G == 2 ? 8 : (G == 4 ? 16 : 24);
+  static constexpr int kNQ = ((HKV * kCS + 15) / 16) * 16;
+  static_assert(kNQ <= 128, "three accumulators of kNQ columns in 512");
+  static constexpr int kPPS = 8 / HKV;  // pages per 128-row stage
+  static constexpr int kMaxTok = 128;
+  static constexpr int kMaxPages = kMaxTok / 16;
+  static constexpr int kThreads = 256;
+  static constexpr int kRowBytes = ((kNQ * 128 + 1023) / 1024) * 1024;  // q digit / P tile
+  static constexpr int kMetaPhys = 0;                                  // int [kMaxPages]
+  static constexpr int kMetaKs = kMetaPhys + kMaxPages * 4;            // float [page][HKV]
+  static constexpr int kMetaVs = kMetaKs + kMaxPages * HKV * 4;        // float [page][HKV]
+  static constexpr int kMetaVmax = kMetaVs + kMaxPages * HKV * 4;      // float [HKV]
+  static constexpr int kMetaT = kMetaVmax + 32;                        // int
+  static constexpr int kMetaBytes = (kMetaT + 16 + 15) & ~15;
+  // chunk tables in flight: the table warp runs this many chunks ahead of the
+  // copies, so its loads (which queue behind the SM's page stream) stay off
+  // the critical path
+  static constexpr int kMetaRing = 4;
+  static constexpr int kNumBars = 2 * 10 + 2 * kMetaRing + 2 * 2 + 2 * 2 + 2 * 2 + 2;
+  static constexpr int kFixed = 4 * kRowBytes + kHeads * kMaxTok * 4 + kMetaRing * kMetaBytes +
+                                2 * 32 * 4 + 3 * kHeads * 8 + 2 * 8 * G * 4 + (kStreamMaxSeqs + 1) * 4 + 64 + 16 +
+                                kNumBars * 8;
+  static constexpr int kMaxDynSmem = 227 * 1024;
+  static constexpr int kStagesFit = (kMaxDynSmem - 1024 - kFixed) / kStageBytes;
+  static constexpr int kStages = kStagesFit < 10 ? kStagesFit : 10;
+  static_assert(kStages >= 4, "ring stages");
+  static constexpr int kOffQ = kStages * kStageBytes;               // [2] digit tiles
+  static constexpr int kOffP = kOffQ + 2 * kRowBytes;               // [2] probability tiles
+  static constexpr int kOffLogit = kOffP + 2 * kRowBytes;           // [kHeads][kMaxTok]
+  static constexpr int kOffMeta = kOffLogit + kHeads * kMaxTok * 4; // [kMetaRing] chunk tables
+  static constexpr int kOffQs = kOffMeta + kMetaRing * kMetaBytes;  // float [2][32] query scales
+  static constexpr int kOffRun = kOffQs + 2 * 32 * 4;               // float2 [kHeads] running (m, l)
+  static constexpr int kOffChunk = kOffRun + kHeads * 8;            // float2 [kHeads] chunk (m, l)
+  static constexpr int kOffAB = kOffChunk + kHeads * 8;             // float2 [kHeads] merge factors
+  static constexpr int kOffHalf = kOffAB + kHeads * 8;              // float [2][8][G] half-warp max / sum
+  static constexpr int kOffPseq = kOffHalf + 2 * 8 * G * 4;         // int [kStreamMaxSeqs + 1]
+  static constexpr int kOffTmp = kOffPseq + (kStreamMaxSeqs + 1) * 4;  // int [16]
+  static constexpr int kOffTmem = ((kOffTmp + 64) + 15) & ~15;
+  static constexpr int kOffBar = kOffTmem + 16;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 1024;
+  static_assert(kSmemBytes <= kMaxDynSmem, "shared memory");
+  static_assert(kOffQ % 1024 == 0 && kOffP % 1024 == 0, "MMA operand tiles: 1 KB alignment");
+  static_assert(kOffMeta % 16 == 0 && kOffBar % 8 == 0, "alignment");
+  // tensor memory: D1 double-buffered, then D2
+  static constexpr int kD2Col = 2 * kNQ;
+  static constexpr int kCols = 3 * kNQ;
+  static constexpr int kTmemCols = kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512);
+  static_assert(kCols <= 512, "tensor memory");
+};
+
+// Loads W consecutive TMEM columns (W in 8, 16, 24, 32, 48; taddr 16-column
+// aligned) of this warp's 32 lanes.
+template <int W>
+__device__ __forceinline__ void tmem_cols(uint32_t taddr, uint32_t (&r)[W]) {
+  if constexpr (W == 8 || W == 16 || W == 32) {
+    tmem_load<W>(taddr, r);
+  } else if constexpr (W == 24) {
+    uint32_t a[16], b[8];
+    tmem_load<16>(taddr, a);
+    tmem_load<8>(taddr + 16, b);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = a[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[16 + i] = b[i];
+  } else {
+    static_assert(W == 48, "TMEM load width");
+    uint32_t a[32], b[16];
+    tmem_load<32>(taddr, a);
+    tmem_load<16>(taddr + 32, b);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = a[i];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[32 + i] = b[i];
+  }
+}
+
+__device__ __forceinline__ float digits_value(uint32_t c0, uint32_t c1, uint32_t c2) {
+  return (float)(int)c2 * 65536.0f + ((float)(int)c1 * 256.0f + (float)(int)c0);
+}
+
+template <int HKV, int G>
+__global__ void __launch_bounds__(256, 1)
+    decode_tcp_kernel(const __grid_constant__ CUtensorMap map_k,
+                      const __grid_constant__ CUtensorMap map_v, const float* __restrict__ q,
+                      const float* __restrict__ k_scale, const float* __restrict__ v_scale,
+                      const int32_t* __restrict__ block_tables,
+                      const int32_t* __restrict__ seq_lens, float* __restrict__ out,
+                      float* __restrict__ ws_acc, float2* __restrict__ ws_ml,
+                      unsigned long long* __restrict__ unit_arrivals, int num_seqs,
+                      int num_heads, int64_t num_blocks, int max_blocks_per_seq, float qk_scale,
+                      int min_pages, int unit_cost, unsigned long long launch_tag, int* err) {
+  using C = TcpCfg<HKV, G>;
+  constexpr int NQ = C::kNQ;
+  constexpr int S = C::kStages;
+  constexpr int BS = 16;
+  constexpr int NH = C::kHeads;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* s_logit = reinterpret_cast<float*>(smem + C::kOffLogit);
+  float2* s_run = reinterpret_cast<float2*>(smem + C::kOffRun);
+  float2* s_chunk = reinterpret_cast<float2*>(smem + C::kOffChunk);
+  float2* s_ab = reinterpret_cast<float2*>(smem + C::kOffAB);
+  float* s_half = reinterpret_cast<float*>(smem + C::kOffHalf);  // [2][8][G]
+  int* s_pseq = reinterpret_cast<int*>(smem + C::kOffPseq);
+  int* s_tmp = reinterpret_cast<int*>(smem + C::kOffTmp);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::kOffTmem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
+  uint64_t* empty = full + S;
+  constexpr int R = C::kMetaRing;
+  uint64_t* meta_full = empty + S;      // [R] chunk table filled (warp 2)
+  uint64_t* meta_free = meta_full + R;  // [R] TMA and epilogue done with it
+  uint64_t* q_full = meta_free + R;     // [2] a sequence's query digits and scales (warp 3)
+  uint64_t* q_free = q_full + 2;        // [2] MMA (commit) and epilogue done with them
+  uint64_t* d1_full = q_free + 2;       // [2] q.K of a stage committed
+  uint64_t* d1_free = d1_full + 2;      // [2] the epilogue has read that D1
+  uint64_t* p_full = d1_free + 2;       // [2] a probability tile written
+  uint64_t* p_free = p_full + 2;        // [2] p.V of that tile committed
+  uint64_t* d2_full = p_free + 2;       // p.V of a chunk committed
+  uint64_t* d2_free = d2_full + 1;      // the epilogue has read D2
+  auto meta = [&](int b) { return smem + C::kOffMeta + b * C::kMetaBytes; };
+  float* s_qs = reinterpret_cast<float*>(smem + C::kOffQs);  // [2][32]
+  auto qtile = [&](int b) { return smem + C::kOffQ + b * C::kRowBytes; };
+  auto ptile = [&](int b) { return smem + C::kOffP + b * C::kRowBytes; };
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S_ = num_seqs;
+  const int grid_ctas = gridDim.x;
+
+  // ---- virtual pages per sequence and their prefix (every CTA, identically)
+  constexpr int kPer = (kStreamMaxSeqs + C::kThreads - 1) / C::kThreads;
+  int mine[kPer];
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int s = tid * kPer + i;
+    mine[i] = 0;
+    if (s < S_) {
+      const int L = seq_lens[s];
+      const int pages = covered_pages(L, BS, max_blocks_per_seq);
+      if (blockIdx.x == 0 && L > pages * BS) record_error(err, kDevSeqTooLong);
+      mine[i] = pages > 0 ? pages + unit_cost : 0;
+    }
+    sum += mine[i];
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) s_tmp[warp] = incl;
+  // query digit and probability tiles: padding rows, and the probability
+  // entries off the block diagonal, stay zero; each chunk rewrites only the
+  // digit rows and its rows' own diagonal probability bytes
+  for (int i = tid; i < 4 * C::kRowBytes / 4; i += C::kThreads)
+    reinterpret_cast<uint32_t*>(smem + C::kOffQ)[i] = 0u;
+  fence_proxy_async_smem();
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < R; ++i) {
+      mbar_init(&meta_full[i], 1);
+      mbar_init(&meta_free[i], 2);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_free[i], 2);
+      mbar_init(&d1_full[i], 1);
+      mbar_init(&d1_free[i], 1);
+      mbar_init(&p_full[i], 1);
+      mbar_init(&p_free[i], 1);
+    }
+    mbar_init(d2_full, 1);
+    mbar_init(d2_free, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(s_tmem, C::kTmemCols);
+  tmem_fence_before_sync();
+  __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tmem = *s_tmem;
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += s_tmp[w];
+  int run = before + incl - sum;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int s = tid * kPer + i;
+    if (s <= S_) s_pseq[s] = run;
+    run += mine[i];
+  }
+  __syncthreads();
+  for (int s = blockIdx.x; s < S_; s += grid_ctas) {  // sequences without pages: zeros
+    if (s_pseq[s + 1] != s_pseq[s]) continue;
+    float4* o = reinterpret_cast<float4*>(out + (int64_t)s * num_heads * 128);
+    for (int i = tid; i < num_heads * 32; i += C::kThreads) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const long long P = (long long)s_pseq[S_];  // one unit (group) per sequence
+  const int n_ctas = (int)min((long long)grid_ctas, max(1LL, (P + min_pages - 1) / min_pages));
+  const long long c_begin = P * blockIdx.x / n_ctas;
+  const long long c_end = P * (blockIdx.x + 1) / n_ctas;
+  const bool active = blockIdx.x < n_ctas && c_begin < c_end;
+  StreamIter it;
+  it.init(active ? c_begin : 0, active ? c_end : 0, s_pseq, S_, 1, C::kMaxPages, unit_cost);
+  StreamChunk ch;
+
+  if (warp == 2) {
+    // ---- chunk tables (block ids, scales, token count), up to R chunks ahead
+    // of the copies.  Under the full page stream an L2 round trip takes
+    // microseconds (responses queue behind the SM's copies), so the loads are
+    // pipelined: the block ids of the next chunk go out with the scales of
+    // this one, and both are in flight while the warp waits for a free table.
+    StreamIter ahead = it;  // one chunk ahead: block ids
+    StreamChunk nx;
+    int v_next = -1, L_next = 0;
+    if (ahead.next(nx)) {
+      if (lane < nx.np) v_next = block_tables[(int64_t)nx.s * max_blocks_per_seq + nx.lp0 + lane];
+      if (lane == 0) L_next = seq_lens[nx.s];
+    }
+    int i = 0;
+    while (it.next(ch)) {
+      const int m = i % R;
+      int phys = -1;
+      if (lane < ch.np) {
+        const bool okb = v_next >= 0 && (int64_t)v_next < num_blocks;
+        if (!okb) record_error(err, kDevBadBlockId);
+        phys = okb ? v_next : -1;
+      }
+      const int Ls = L_next;
+      float ks[HKV], vs[HKV];
+#pragma unroll
+      for (int h = 0; h < HKV; ++h) {
+        ks[h] = phys >= 0 ? k_scale[(int64_t)phys * HKV + h] : 0.0f;
+        vs[h] = phys >= 0 ? v_scale[(int64_t)phys * HKV + h] : 0.0f;
+      }
+      v_next = -1;
+      L_next = 0;
+      if (ahead.next(nx)) {
+        if (lane < nx.np)
+          v_next = block_tables[(int64_t)nx.s * max_blocks_per_seq + nx.lp0 + lane];
+        if (lane == 0) L_next = seq_lens[nx.s];
+      }
+      if (i >= R) {
+        bool ok = true;
+        if (lane == 0 && !mbar_wait_bounded(&meta_free[m], (uint32_t)((i / R) - 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok = false;
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      uint8_t* mt = meta(m);
+      if (lane < ch.np) reinterpret_cast<int*>(mt + C::kMetaPhys)[lane] = phys;
+#pragma unroll
+      for (int h = 0; h < HKV; ++h) {
+        if (lane < ch.np) {
+          reinterpret_cast<float*>(mt + C::kMetaKs)[lane * HKV + h] = ks[h];
+          reinterpret_cast<float*>(mt + C::kMetaVs)[lane * HKV + h] = vs[h];
+        }
+        const float vm = warp_max(vs[h]);
+        if (lane == 0) reinterpret_cast<float*>(mt + C::kMetaVmax)[h] = vm;
+      }
+      if (lane == 0) {
+        const int pages = s_pseq[ch.s + 1] - s_pseq[ch.s] - unit_cost;
+        const int L = min(max(Ls, 0), pages * BS);
+        *reinterpret_cast<int*>(mt + C::kMetaT) = min(L, (ch.lp0 + ch.np) * BS) - ch.lp0 * BS;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_full[m]);
+      ++i;
+    }
+  } else if (warp == 3) {
+    // ---- query digit tiles, one per sequence (its chunks are consecutive),
+    // in a ring of two: the digits are computed into registers before the
+    // warp waits for a free tile, so only the shared-memory stores follow it
+    constexpr int kBatch = NH < 8 ? NH : 8;  // query rows in flight per lane
+    int j = -1, prev_s = -1;
+    while (it.next(ch)) {
+      if (ch.s == prev_s) continue;
+      prev_s = ch.s;
+      ++j;
+      const int qb = j & 1;
+      uint32_t dg[NH][3];
+      float my_qs = 0.0f;  // lane hq: the scale of query head hq
+#pragma unroll
+      for (int h0 = 0; h0 < NH; h0 += kBatch) {
+        float4 xq[kBatch];
+#pragma unroll
+        for (int t = 0; t < kBatch; ++t)
+          xq[t] = reinterpret_cast<const float4*>(
+              q + ((int64_t)ch.s * num_heads + h0 + t) * 128)[lane];
+#pragma unroll
+        for (int t = 0; t < kBatch; ++t) {
+          const float4 x = xq[t];
+          float mx = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+          mx = warp_max(mx);
+          const float inv = mx > 0.0f ? (float)kQFix / mx : 0.0f;
+          const float xs[4] = {x.x, x.y, x.z, x.w};
+          int d[4][3];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            int n = __float2int_rn(xs[e] * inv);
+            n = max(-kQFix, min(kQFix, n));
+            to_digits(n, d[e][0], d[e][1], d[e][2]);
+          }
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl) dg[h0 + t][pl] = pack4(d[0][pl], d[1][pl], d[2][pl], d[3][pl]);
+          if (lane == h0 + t) my_qs = mx > 0.0f ? mx / (float)kQFix : 0.0f;
+        }
+      }
+      if (j >= 2) {
+        bool ok = true;
+        if (lane == 0 && !mbar_wait_bounded(&q_free[qb], (uint32_t)((j >> 1) - 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok = false;
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      uint8_t* sq = qtile(qb);
+#pragma unroll
+      for (int hq = 0; hq < NH; ++hq)
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl)
+          *reinterpret_cast<uint32_t*>(
+              sq + sw128_offset((hq / G) * C::kCS + 3 * (hq % G) + pl, 4 * lane)) = dg[hq][pl];
+      if (lane < NH) s_qs[qb * 32 + lane] = my_qs;
+      fence_proxy_async_smem();  // an MMA operand
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_full[qb]);
+    }
+  } else if (warp == 0) {
+    // ---- TMA: the chunk's K stages, then its V stages; lane 0 arms each
+    // stage, lane j issues page j of it (one box per page)
+    const uint64_t policy = l2_policy_evict_first();
+    if (lane == 0) {
+      prefetch_tensormap(&map_k);
+      prefetch_tensormap(&map_v);
+    }
+    int i = 0, ns = 0;
+    bool ok_run = true;
+    while (ok_run && it.next(ch)) {
+      const int m = i % R;
+      bool ok = true;
+      if (lane == 0 && !mbar_wait_bounded(&meta_full[m], (uint32_t)(i / R) & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        ok = false;
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int* phys_t = reinterpret_cast<const int*>(meta(m) + C::kMetaPhys);
+      const int n_st = (ch.np + C::kPPS - 1) / C::kPPS;
+      for (int kind = 0; kind < 2 && ok_run; ++kind) {
+        for (int st = 0; st < n_st; ++st, ++ns) {
+          const int slot = ns % S;
+          const int pb = st * C::kPPS, pe = min(ch.np, pb + C::kPPS);
+          bool oks = true;
+          if (lane == 0) {
+            if (!mbar_wait_bounded(&empty[slot], ((uint32_t)(ns / S) & 1u) ^ 1u, err)) {
+              record_error(err, kDevWaitTimeout);
+              oks = false;
+            } else {
+              mbar_arrive_expect_tx(&full[slot], (uint32_t)((pe - pb) * BS * HKV * 128));
+            }
+          }
+          oks = __shfl_sync(0xffffffffu, oks, 0);
+          __syncwarp();  // the stage is armed before any of its copies is issued
+          if (!oks) {
+            ok_run = false;
+            break;
+          }
+          if (lane < pe - pb)
+            tma_load_4d(smem + slot * kStageBytes + lane * BS * HKV * 128, kind ? &map_v : &map_k,
+                        &full[slot], 0, 0, 0, max(phys_t[pb + lane], 0), policy);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_free[m]);
+      ++i;
+    }
+    if (lane == 0) drain_ring(full, S, ns);  // no copy outlives the CTA
+  } else if (warp == 1) {
+    // ---- MMA issue: per chunk q.K of each K stage into D1 (alternating
+    // buffers), then p.V of each V stage into D2 ----------------------------
+    if (lane == 0) {
+      constexpr uint32_t kIdQK = umma_i8_idesc(1, 1, 0, 0, 128, NQ);
+      constexpr uint32_t kIdPV = umma_i8_idesc(1, 0, 1, 0, 128, NQ);
+      const uint32_t stage0 = smem_u32(smem);
+      int i = 0, ns = 0, kd = 0, pv = 0, j = -1, prev_s = -1;
+      uint64_t* last_bar = nullptr;  // the last d1_full / d2_full commit, drained at exit
+      uint32_t last_par = 0;
+      bool ok_run = true;
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        if (!mbar_wait_bounded(bar, parity, err)) {
+          record_error(err, kDevWaitTimeout);
+          ok_run = false;
+          return false;
+        }
+        tmem_fence_after_sync();
+        return true;
+      };
+      while (ok_run && it.next(ch)) {
+        const int n_st = (ch.np + C::kPPS - 1) / C::kPPS;
+        if (ch.s != prev_s) {  // a new sequence: release the last digit tile, take the next
+          if (j >= 0) umma_commit(&q_free[j & 1]);
+          prev_s = ch.s;
+          ++j;
+          if (!wait(&q_full[j & 1], (uint32_t)(j >> 1) & 1u)) break;
+        }
+        const uint32_t qaddr = smem_u32(qtile(j & 1));
+        for (int st = 0; st < n_st && ok_run; ++st, ++ns, ++kd) {
+          const int slot = ns % S, db = kd & 1;
+          if (!wait(&full[slot], (uint32_t)(ns / S) & 1u)) break;
+          if (kd >= 2 && !wait(&d1_free[db], (uint32_t)((kd >> 1) - 1) & 1u)) break;
+          const uint32_t a = stage0 + slot * kStageBytes;
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq)
+            umma_i8(tmem + db * NQ, umma_sw128_desc(a + kq * 32, 16, 1024),
+                    umma_sw128_desc(qaddr + kq * 32, 16, 1024), kIdQK, kq > 0);
+          umma_commit(&empty[slot]);
+          umma_commit(&d1_full[db]);
+          last_bar = &d1_full[db];
+          last_par = (uint32_t)(kd >> 1) & 1u;
+        }
+        if (!ok_run) break;
+        if (i >= 1 && !wait(d2_free, (uint32_t)(i - 1) & 1u)) break;
+        for (int st = 0; st < n_st && ok_run; ++st, ++ns, ++pv) {
+          const int slot = ns % S, pb = pv & 1;
+          if (!wait(&full[slot], (uint32_t)(ns / S) & 1u)) break;
+          if (!wait(&p_full[pb], (uint32_t)(pv >> 1) & 1u)) break;
+          const uint32_t a = stage0 + slot * kStageBytes;
+          const uint32_t paddr = smem_u32(ptile(pb));
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq)
+            umma_i8(tmem + C::kD2Col, umma_sw128_desc(a + kq * 4096, 16, 1024),
+                    umma_sw128_desc(paddr + kq * 32, 16, 1024), kIdPV,
+                    (st > 0 || kq > 0) ? 1u : 0u);
+          umma_commit(&empty[slot]);
+          umma_commit(&p_free[pb]);
+        }
+        if (!ok_run) break;
+        umma_commit(d2_full);
+        last_bar = d2_full;
+        last_par = (uint32_t)i & 1u;
+        ++i;
+      }
+      // every MMA of this thread is done before TMEM is freed
+      if (last_bar != nullptr) mbar_drain(last_bar, last_par);
+    }
+  } else if (warp >= 4) {
+    // ---- epilogue: TMEM lane e is a stage row for D1 and a head dimension
+    // for D2 -------------------------------------------------------------------
+    constexpr int CS = C::kCS;
+    constexpr int W1 = HKV >= 2 ? 2 * CS : CS;  // D1 columns a warp reads (its two heads)
+    const int e = tid - 128;
+    const int w4 = warp - 4;
+    const uint32_t lane_base = (uint32_t)(32 * w4) << 16;
+    const int h_e = (e >> 4) % HKV;   // the row's KV head
+    const int pp_e = e / (16 * HKV);  // its page within the stage
+    const int t_e = e & 15;           // its token within the page
+    const int hw = e >> 4;            // half-warp 0..7 (head hw % HKV)
+    const bool upper = HKV >= 2 && (lane >> 4) != 0;
+    const int hcol = HKV >= 2 ? (2 * w4) % HKV : 0;  // the warp's first head
+    float acc_run[NH];
+#pragma unroll
+    for (int hq = 0; hq < NH; ++hq) acc_run[hq] = 0.0f;
+    int i = 0, kd = 0, pv = 0, j = -1, prev_s = -1;
+    bool live = true;
+    while (it.next(ch)) {
+      const int b = i % R;
+      const uint8_t* m = meta(b);
+      const int* phys_t = reinterpret_cast<const int*>(m + C::kMetaPhys);
+      const float* ks_t = reinterpret_cast<const float*>(m + C::kMetaKs);
+      const float* vs_t = reinterpret_cast<const float*>(m + C::kMetaVs);
+      const float* vmax_t = reinterpret_cast<const float*>(m + C::kMetaVmax);
+      if (ch.s != prev_s) {
+        // a new sequence: every thread finished the last one's query scales
+        // at the barriers that ended its chunk
+        if (j >= 0 && e == 0) mbar_arrive(&q_free[j & 1]);
+        prev_s = ch.s;
+        ++j;
+        if (live && !mbar_wait_bounded(&q_full[j & 1], (uint32_t)(j >> 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          live = false;
+        }
+      }
+      const float* qs_t = s_qs + (j & 1) * 32;
+      if (live && !mbar_wait_bounded(&meta_full[b], (uint32_t)(i / R) & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
+      }
+      const int T = live ? *reinterpret_cast<const int*>(m + C::kMetaT) : 0;
+      const int n_st = (ch.np + C::kPPS - 1) / C::kPPS;
+
+      // ---- K phase: logits of this row's query heads, running maxima
+      float kmax[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) kmax[g] = -INFINITY;
+      for (int st = 0; st < n_st; ++st, ++kd) {
+        const int db = kd & 1;
+        if (live && !mbar_wait_bounded(&d1_full[db], (uint32_t)(kd >> 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          live = false;
+        }
+        tmem_fence_after_sync();
+        const int pg = st * C::kPPS + pp_e;
+        const int tok = pg * 16 + t_e;
+        const bool valid = live && pg < ch.np && tok < T && phys_t[pg] >= 0;
+        const float ksc = pg < ch.np ? ks_t[pg * HKV + h_e] : 0.0f;
+        uint32_t r[W1];
+        tmem_cols<W1>(tmem + lane_base + db * NQ + hcol * CS, r);
+        tmem_wait_load();
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float v = digits_value(r[3 * g], r[3 * g + 1], r[3 * g + 2]);
+          if constexpr (HKV >= 2) {
+            const float hi = digits_value(r[CS + 3 * g], r[CS + 3 * g + 1], r[CS + 3 * g + 2]);
+            v = upper ? hi : v;
+          }
+          const float logit = valid ? v * (qs_t[h_e * G + g] * ksc * qk_scale) : -INFINITY;
+          s_logit[(h_e * G + g) * C::kMaxTok + tok] = logit;
+          kmax[g] = fmaxf(kmax[g], logit);
+        }
+        tmem_fence_before_sync();
+        named_barrier(1, 128);  // every row of D1 read
+        if (e == 0) mbar_arrive(&d1_free[db]);
+      }
+      // ---- the chunk's maximum per (KV head, query head): half-warps hold
+      // 16 rows of one head; heads repeat over the stage's pages
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float mm = kmax[g];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        if ((lane & 15) == 0) s_half[hw * G + g] = mm;
+      }
+      named_barrier(1, 128);
+      if (e < NH) {
+        float mm = -INFINITY;
+        for (int j = e / G; j < 8; j += HKV) mm = fmaxf(mm, s_half[j * G + e % G]);
+        s_chunk[e].x = mm;
+      }
+      named_barrier(1, 128);
+
+      // ---- V phase: one block-diagonal probability tile per V stage
+      const float vmax_e = vmax_t[h_e];
+      const float to_fix = vmax_e > 0.0f ? 16777215.0f / vmax_e : 0.0f;
+      float mh[G], lsum[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        mh[g] = s_chunk[h_e * G + g].x;
+        lsum[g] = 0.0f;
+      }
+      for (int st = 0; st < n_st; ++st, ++pv) {
+        const int pb = pv & 1;
+        if (pv >= 2 && live &&
+            !mbar_wait_bounded(&p_free[pb], (uint32_t)((pv >> 1) - 1) & 1u, err)) {
+          record_error(err, kDevWaitTimeout);
+          live = false;
+        }
+        const int pg = st * C::kPPS + pp_e;
+        const int tok = pg * 16 + t_e;
+        const bool valid = pg < ch.np && tok < T;
+        const float vs = pg < ch.np ? vs_t[pg * HKV + h_e] : 0.0f;
+        uint8_t* pt = ptile(pb);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          uint32_t n = 0;
+          if (valid && mh[g] != -INFINITY) {
+            const float p = exp2f(s_logit[(h_e * G + g) * C::kMaxTok + tok] - mh[g]);
+            lsum[g] += p;
+            n = __float2uint_rn(fminf(p * vs * to_fix, 16777215.0f));
+          }
+          const int row = h_e * CS + 3 * g;
+          pt[sw128_offset(row, e)] = (uint8_t)(n & 255u);
+          pt[sw128_offset(row + 1, e)] = (uint8_t)((n >> 8) & 255u);
+          pt[sw128_offset(row + 2, e)] = (uint8_t)(n >> 16);
+        }
+        fence_proxy_async_smem();
+        named_barrier(1, 128);
+        if (e == 0) mbar_arrive(&p_full[pb]);
+      }
+      // ---- the chunk's sums, then the merge factors with the running (m, l)
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float ls = lsum[g];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+        if ((lane & 15) == 0) s_half[8 * G + hw * G + g] = ls;
+      }
+      named_barrier(1, 128);
+      if (e < NH) {
+        float l = 0.0f;
+        for (int j = e / G; j < 8; j += HKV) l += s_half[8 * G + j * G + e % G];
+        const float mc = s_chunk[e].x;
+        if (ch.seg_first) {
+          s_ab[e] = make_float2(0.0f, 1.0f);
+          s_run[e] = make_float2(mc, l);
+        } else {
+          const float2 rr = s_run[e];
+          const float M = fmaxf(rr.x, mc);
+          const float a = rr.x == -INFINITY ? 0.0f : exp2f(rr.x - M);
+          const float bb = mc == -INFINITY ? 0.0f : exp2f(mc - M);
+          s_ab[e] = make_float2(a, bb);
+          s_run[e] = make_float2(M, rr.y * a + l * bb);
+        }
+      }
+      if (live && !mbar_wait_bounded(d2_full, (uint32_t)i & 1u, err)) {
+        record_error(err, kDevWaitTimeout);
+        live = false;
+      }
+      tmem_fence_after_sync();
+      named_barrier(1, 128);  // s_ab, s_run published
+      // ---- D2: this thread's dimension e of every query head's result
+#pragma unroll
+      for (int hp = 0; hp < (HKV >= 2 ? HKV / 2 : 1); ++hp) {
+        uint32_t r[W1];
+        tmem_cols<W1>(tmem + lane_base + C::kD2Col + hp * W1, r);
+        tmem_wait_load();
+#pragma unroll
+        for (int hh = 0; hh < (HKV >= 2 ? 2 : 1); ++hh) {
+          const int h = hp * 2 + hh;
+          const float back = vmax_t[h] * (1.0f / 16777215.0f);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const int hq = h * G + g;
+            const float accc =
+                digits_value(r[hh * CS + 3 * g], r[hh * CS + 3 * g + 1], r[hh * CS + 3 * g + 2]) *
+                back;
+            const float2 ab = s_ab[hq];
+            acc_run[hq] = acc_run[hq] * ab.x + ab.y * accc;
+          }
+        }
+      }
+      tmem_fence_before_sync();
+      named_barrier(1, 128);  // D2 and the table half read
+      if (e == 0) {
+        mbar_arrive(d2_free);
+        mbar_arrive(&meta_free[b]);
+      }
+
+      // ---- end of this CTA's part of the unit: write it
+      if (ch.seg_last) {
+        const int u = ch.s;  // one unit per sequence
+        if (ch.whole) {
+#pragma unroll
+          for (int hq = 0; hq < NH; ++hq) {
+            const float l = s_run[hq].y;
+            out[((int64_t)ch.s * num_heads + hq) * 128 + e] = l > 0.0f ? acc_run[hq] / l : 0.0f;
+          }
+        } else {
+#pragma unroll
+          for (int hq = 0; hq < NH; ++hq) {
+            const int64_t slot = ((int64_t)u + blockIdx.x) * NH + hq;
+            ws_acc[slot * 128 + e] = acc_run[hq];
+            if (e == 0) ws_ml[slot] = s_run[hq];
+          }
+          int first, last;
+          unit_owners(s_pseq, ch.s, 0, 1, unit_cost, P, n_ctas, first, last);
+          const int nseg = last - first + 1;
+          const int ngroups = (nseg + kMergeGroup - 1) / kMergeGroup;
+          const int g_lo = first + (int)(blockIdx.x - first) / kMergeGroup * kMergeGroup;
+          const int g_hi = min(last, g_lo + kMergeGroup - 1);
+          // every partial store of this CTA is ordered before thread e == 0's
+          // release by the barrier; the last arrival acquires all of them
+          named_barrier(1, 128);
+          if (e == 0) {
+            const int r = ngroups == 1
+                              ? arrive_on_unit(&unit_arrivals[u], launch_tag, nseg, 0ull)
+                              : arrive_on_unit(&unit_arrivals[S_ + u + g_lo], launch_tag,
+                                               g_hi - g_lo + 1, 0ull);
+            if (r < 0) record_error(err, kDevWaitTimeout);
+            s_tmp[8] = r == 1;
+          }
+          named_barrier(1, 128);
+          int m_lo = g_lo, m_n = g_hi - g_lo + 1, m_stride = 1;
+          bool final_pass = ngroups == 1;
+          bool merging = s_tmp[8] != 0;
+          while (merging) {
+#pragma unroll 1
+            for (int hq = w4; hq < NH; hq += 4) {
+              float4 a;
+              float M, den;
+              merge_partials(ws_acc, ws_ml, m_n, lane, a, M, den, [&](int j) {
+                return ((int64_t)u + m_lo + j * m_stride) * NH + hq;
+              });
+              if (final_pass) {
+                const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+                reinterpret_cast<float4*>(out + ((int64_t)ch.s * num_heads + hq) * 128)[lane] =
+                    make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+              } else {
+                const int64_t slot = ((int64_t)u + g_lo) * NH + hq;
+                reinterpret_cast<float4*>(ws_acc + slot * 128)[lane] = a;
+                if (lane == 0) ws_ml[slot] = make_float2(M, den);
+              }
+            }
+            if (final_pass) break;
+            named_barrier(1, 128);  // the group's partial is stored
+            if (e == 0) {
+              const int r = arrive_on_unit(&unit_arrivals[u], launch_tag, ngroups, 0ull);
+              if (r < 0) record_error(err, kDevWaitTimeout);
+              s_tmp[9] = r == 1;
+            }
+            named_barrier(1, 128);
+            merging = s_tmp[9] != 0;
+            m_lo = first;
+            m_n = ngroups;
+            m_stride = kMergeGroup;
+            final_pass = true;
+          }
+        }
+#pragma unroll
+        for (int hq = 0; hq < NH; ++hq) acc_run[hq] = 0.0f;
+      }
+      ++i;
+    }
+  }
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// ===========================================================================
 // Planning and dispatch
 // ===========================================================================
 
@@ -2501,6 +3272,7 @@ struct Plan {
   bool fast = false;
   bool tc = false;      // tensor-core GQA kernel (bs 16, group 2/4/8)
   bool stream = false;  // persistent balanced kernel (fast shapes, S <= 1024)
+  bool tcp = false;     // whole-page tensor-core stream kernel (a stream plan too)
   int hg = 1, g = 1;
   int pages_per_split = 1;
   int max_splits = 1;
@@ -2569,6 +3341,25 @@ Plan make_plan(const DecodeArgs& a) {
   }
   if (p.fast && a.block_size == 16 && (group == 2 || group == 4 || group == 8) &&
       env_int("PKV_DECODE_TC", 1) != 0) {
+    const int hkv = a.num_kv_heads;
+    const int cs = group == 2 ? 8 : (group == 4 ? 16 : 24);
+    if ((hkv == 1 || hkv == 2 || hkv == 4 || hkv == 8) && hkv * cs <= 128 &&
+        a.num_seqs <= kStreamMaxSeqs && env_int("PKV_DECODE_TC_PAGES", 0) != 0 &&
+        env_int("PKV_DECODE_TC_SPLIT", 0) == 0) {
+      // whole pages on the tensor cores, the stream kernel's scheduling (on
+      // request: measured slower than the per-head kernel below, since one
+      // CTA per SM keeps at most 8 pages of 16 KB in flight)
+      p.tcp = true;
+      p.stream = true;
+      p.hg = hkv;
+      p.g = group;
+      const int forced = env_int("PKV_DECODE_CTAS", 0);
+      p.n_ctas = forced > 0 ? forced : sm_count();
+      p.min_pages = std::max(1, env_int("PKV_STREAM_MIN_PAGES", 4));
+      p.unit_cost = std::max(0, env_int("PKV_STREAM_UNIT_COST", 4));
+      p.max_splits = 1;
+      return p;
+    }
     // one CTA per (sequence, KV head, split of 8..32 pages)
     p.tc = true;
     int pps = group <= 4 ? TcCfg<4>::kMaxPages : TcCfg<8>::kMaxPages;
@@ -2697,6 +3488,41 @@ int launch_tc_t(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_ml
   return kOk;
 }
 
+template <int HKV, int G>
+int launch_tcp_t(const DecodeArgs& a, const Plan& p, float* ws_base, cudaStream_t stream) {
+  using C = TcpCfg<HKV, G>;
+  CUtensorMap mk, mv;
+  if (!cached_cache_map(&mk, a.k_cache, a.num_blocks, 16, HKV, -1) ||
+      !cached_cache_map(&mv, a.v_cache, a.num_blocks, 16, HKV, -1)) {
+    set_error("cuTensorMapEncodeTiled failed for the paged cache (page map)");
+    return kCudaError;
+  }
+  auto kern = decode_tcp_kernel<HKV, G>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  const StreamWs w = stream_ws_layout(a, p);
+  uint8_t* base = reinterpret_cast<uint8_t*>(ws_base);
+  kern<<<p.n_ctas, C::kThreads, C::kSmemBytes, stream>>>(
+      mk, mv, a.q, a.k_scale, a.v_scale, a.block_tables, a.seq_lens, a.out,
+      reinterpret_cast<float*>(base + w.acc_off), reinterpret_cast<float2*>(base + w.ml_off),
+      reinterpret_cast<unsigned long long*>(base + w.cnt_off), a.num_seqs, a.num_heads,
+      a.num_blocks, a.max_blocks_per_seq, a.sm_scale * kLog2e, std::max(1, p.min_pages),
+      std::max(0, p.unit_cost), next_launch_tag(), device_error_word());
+  return kOk;
+}
+
+int launch_tcp(const DecodeArgs& a, const Plan& p, float* ws_base, cudaStream_t stream) {
+  const int g = a.num_heads / a.num_kv_heads;
+#define PKV_TCP(H, GG) \
+  if (a.num_kv_heads == H && g == GG) return launch_tcp_t<H, GG>(a, p, ws_base, stream);
+  PKV_TCP(8, 2) PKV_TCP(8, 4)
+  PKV_TCP(4, 2) PKV_TCP(4, 4) PKV_TCP(4, 8)
+  PKV_TCP(2, 2) PKV_TCP(2, 4) PKV_TCP(2, 8)
+  PKV_TCP(1, 2) PKV_TCP(1, 4) PKV_TCP(1, 8)
+#undef PKV_TCP
+  set_error("internal: no whole-page tensor-core instantiation for this head layout");
+  return kUnsupported;
+}
+
 int launch_tc(const DecodeArgs& a, const Plan& p, float* ws_acc, float2* ws_ml,
               cudaStream_t stream) {
   switch (a.num_heads / a.num_kv_heads) {
@@ -2782,8 +3608,9 @@ int launch_decode(const DecodeArgs& a, void* workspace, size_t workspace_bytes,
     }
     ws_acc = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(workspace) + 255) &
                                       ~(uintptr_t)255);
-    const int rc = a.block_size == 16 ? dispatch_hg<16>(a, p, ws_acc, nullptr, stream)
-                                      : dispatch_hg<32>(a, p, ws_acc, nullptr, stream);
+    const int rc = p.tcp ? launch_tcp(a, p, ws_acc, stream)
+                   : a.block_size == 16 ? dispatch_hg<16>(a, p, ws_acc, nullptr, stream)
+                                        : dispatch_hg<32>(a, p, ws_acc, nullptr, stream);
     if (rc != kOk) return rc;
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -107,12 +107,15 @@ def test_decode_kernel_launches_per_call(lib, monkeypatch):
     monkeypatch.delenv("PKV_DECODE_SPLIT", raising=False)
     monkeypatch.delenv("PKV_DECODE_GENERIC", raising=False)
     assert f(64, 8, 8, 128, 16, 128) == 1      # persistent stream kernel
-    assert f(512, 32, 8, 128, 16, 512) == 2    # GQA group of 4: tensor-core kernel + combine
+    assert f(512, 32, 8, 128, 16, 512) == 2    # GQA group of 4: per-head tensor-core + combine
     assert f(512, 24, 8, 128, 16, 512) == 2    # group of 3: generic kernel + combine
     assert f(512, 32, 8, 128, 32, 256) == 1    # group of 4, block_size 32: stream kernel
     assert f(2048, 8, 8, 128, 16, 128) == 2    # > 1,024 sequences: split-K + combine
     assert f(8, 8, 8, 64, 16, 32) == 2         # head_dim 64: generic kernel + combine
     assert f(0, 8, 8, 128, 16, 128) == 0
+    monkeypatch.setenv("PKV_DECODE_TC_PAGES", "1")
+    assert f(512, 32, 8, 128, 16, 512) == 1    # whole-page tensor-core kernel
+    assert f(512, 64, 8, 128, 16, 512) == 2    # group of 8 x 8 KV heads: stays per head
     monkeypatch.setenv("PKV_DECODE_TC", "0")
     assert f(512, 32, 8, 128, 16, 512) == 1    # tensor-core path off: stream kernel
     monkeypatch.setenv("PKV_DECODE_SPLIT", "1")

@@ -343,39 +343,49 @@ def test_attention_stream_one_sequence_over_all_ctas(cuda):
 
 
 def _tc_form(monkeypatch, form):
-    """persistent: three CTAs per SM walking the units (the default);
-    split: one CTA per split."""
+    """persistent: one KV head per unit, three CTAs per SM walking the units
+    (the default); split: one CTA per split (both followed by the combine
+    kernel); page: whole pages per copy, all KV heads of a sequence in one
+    CTA, the stream kernel's scheduling (on request; one launch)."""
     if form == "split":
         monkeypatch.setenv("PKV_DECODE_TC_SPLIT", "1")
+    elif form == "page":
+        monkeypatch.setenv("PKV_DECODE_TC_PAGES", "1")
 
 
-@pytest.mark.parametrize("form", ["persistent", "split"])
+@pytest.mark.parametrize("form", ["page", "persistent", "split"])
 @pytest.mark.parametrize("group", [2, 4, 8])
 @pytest.mark.parametrize("pages", ["auto", "8", "16", "32"])
 def test_attention_tensor_core_gqa(cuda, monkeypatch, form, group, pages):
     """GQA groups of 2/4/8 query heads per KV head run on the tcgen05 kernel
     (q.K and p.V as int8 MMAs into tensor memory); ragged lengths, partial
     128-token tiles, one to four tiles per split, several splits; the
-    persistent form (CTAs walk the units) and the split form (one CTA per
-    split), both followed by the combine kernel."""
+    page, persistent and split forms."""
     if pages != "auto":
         monkeypatch.setenv("PKV_DECODE_SPLIT_PAGES", pages)
     _tc_form(monkeypatch, form)
     from pagedkv_fusion import _C
     for seed, S, hkv, L in ((31, 7, 4, 1500), (32, 3, 2, 130), (33, 12, 8, 700), (34, 2, 1, 17)):
-        assert _C.quant_paged_attention_kernel_launches(S, group * hkv, hkv, 128, 16, 94) == 2
+        # the page form needs Hkv x (8 / 16 / 24 columns for groups of 2 / 4 / 8)
+        # <= 128 accumulator columns; 8 KV heads x groups of 8 stay per head
+        cols = hkv * {2: 8, 4: 16, 8: 24}[group]
+        want_launches = 1 if form == "page" and cols <= 128 else 2
+        assert _C.quant_paged_attention_kernel_launches(S, group * hkv, hkv, 128, 16, 94) == \
+            want_launches
         prob = problems.make_paged_kv_problem(np.random.default_rng(seed), S, group * hkv, hkv,
                                               128, 16, L)
         args = quantized_problem(*prob)
         assert_attention_close(run_attention(args), c_oracle.paged_attention(*args))
 
 
+@pytest.mark.parametrize("form", ["page", "persistent"])
 @pytest.mark.parametrize("group", [2, 4, 8])
-def test_tensor_core_persistent_merge_edges(cuda, group):
+def test_tensor_core_persistent_merge_edges(cuda, monkeypatch, form, group):
     """The tensor-core path with its combine: sequences without pages (zero
     output) and of one page, a long sequence with many splits whose units
     wrap around the persistent grid, repeated calls bit for bit, and a
     workspace of random bytes."""
+    _tc_form(monkeypatch, form)
     r = np.random.default_rng(70 + group)
     hkv = 2
     q, k, v, bt, sl, sm = problems.make_paged_kv_problem(r, 6, group * hkv, hkv, 128, 16, 40000)
@@ -405,18 +415,21 @@ def test_tensor_core_persistent_merge_edges(cuda, group):
 def test_tensor_core_forms_agree_bitwise(cuda, monkeypatch, group):
     """The persistent and split forms run the same arithmetic per unit (same
     MMAs, same epilogue): bit-identical outputs, on a batch that gives every
-    persistent CTA several units."""
+    persistent CTA several units; the page form within the oracle tolerance."""
     prob = problems.make_paged_kv_problem(np.random.default_rng(90 + group), 40, group * 8, 8,
                                           128, 16, 2000)
     args = quantized_problem(*prob)
     want = c_oracle.paged_attention(*args)
     outs = {}
-    for form in ("persistent", "split"):
+    for form in ("page", "persistent", "split"):
         with monkeypatch.context() as mp:
             _tc_form(mp, form)
             outs[form] = run_attention(args)
     assert_attention_close(outs["persistent"], want)
     assert torch.equal(outs["persistent"], outs["split"])
+    # the page form normalizes per 128-token chunk and merges the chunks
+    # online: the same oracle tolerance, not the same bits
+    assert_attention_close(outs["page"], want)
 
 
 def test_attention_tensor_core_matches_cuda_core_path(cuda, monkeypatch):

@@ -11,7 +11,9 @@ two problems of different shapes called back to back, so every call starts
 on the scratch contents the previous one left:
 
 * groups of 2 and 4 query heads per KV head take the tensor-core kernel,
-  whose split partials are merged by a second kernel;
+  whose split partials are merged by a second kernel; on request
+  (PKV_DECODE_TC_PAGES=1) the whole-page tensor-core kernel, one launch,
+  whose arrival counters and partials live in the scratch;
 * one query head per KV head takes the persistent stream kernel (one
   launch per call, asserted), whose launch-tagged arrival counters live in
   the scratch and are not reset between calls.
@@ -104,6 +106,16 @@ def test_noalloc_tensor_core_path_twice():
     if not torch.cuda.is_available():
         pytest.fail("gpu test run without a visible CUDA device")
     _check_twice(_lib(), ((1, (12, 16, 8, 3000)), (2, (5, 32, 8, 1700))), launches=2)
+
+
+def test_noalloc_page_kernel_twice(monkeypatch):
+    """Groups of 2 and 4 on the whole-page tensor-core kernel (one launch):
+    the second problem starts on the counters and partials the first left
+    in the shared scratch."""
+    if not torch.cuda.is_available():
+        pytest.fail("gpu test run without a visible CUDA device")
+    monkeypatch.setenv("PKV_DECODE_TC_PAGES", "1")
+    _check_twice(_lib(), ((1, (12, 16, 8, 3000)), (2, (5, 32, 8, 1700))), launches=1)
 
 
 def test_noalloc_stream_kernel_reuses_its_counters():
