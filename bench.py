@@ -593,15 +593,20 @@ def run_gpu_arm(args):
                        "cross PCIe; wall clock per step, max over ranks"}
 
     # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum)
-    # from one ncu capture of decode_stream_kernel<16, 8, 1> on the heavy-tail
-    # workload: 272,910,336 B for 269,517,056 algorithmic bytes.  A large-head
-    # launch (24 GB resident) is too large to capture; the same kernel streams
-    # the same per-page layout, so its traffic is that ratio times its own
-    # algorithmic bytes.
-    traffic = my_bytes * (272910336 / 269517056)
-    traffic_basis = ("ncu capture of this workload" if args.workload == "heavy-tail"
-                     else "heavy-tail ncu capture's traffic/algorithmic ratio x this "
-                          "workload's algorithmic bytes")
+    # from ncu captures of decode_stream_kernel<16, 8, 1>.  Heavy-tail
+    # workload: 272,910,336 B for 269,517,056 algorithmic bytes.  A
+    # large-head launch (24 GB resident) is too large to capture; a 40/40-head
+    # case of 32 sequences x 4,608 tokens (the same instantiation, five head
+    # groups per sequence) read 1,513,802,752 B and wrote 3,766,272 B for
+    # 1,514,246,272 algorithmic bytes, so the large-head traffic is that ratio
+    # times its own algorithmic bytes (traffic grows with the pages streamed).
+    if args.workload == "heavy-tail":
+        traffic = my_bytes * (272910336 / 269517056)
+        traffic_basis = "ncu capture of this workload"
+    else:
+        traffic = my_bytes * ((1513802752 + 3766272) / 1514246272)
+        traffic_basis = ("ncu capture of a 40/40-head 32 x 4,608-token case of the same kernel: "
+                         "its traffic/algorithmic ratio x this workload's algorithmic bytes")
     launches_per_step = C.quant_paged_attention_kernel_launches(
         len(lens), heads, kv_heads, HEAD_DIM, BLOCK, bt_np.shape[1])
     plan_name = ("persistent decode_stream_kernel" if launches_per_step == 1

@@ -850,34 +850,43 @@ __device__ __forceinline__ void merge_partials(const float* __restrict__ ws_acc,
 
 // Arrival counters need no reset before a launch, and no CTA waits for
 // another to prepare them.  A counter holds (launch tag << kArrivalBits) |
-// arrivals.  Each arrival is one compare-and-swap (acquire-release, GPU
-// scope): a counter that carries this launch's tag gets one more arrival; a
-// counter with any other tag -- 0 after a completed set, or what an earlier
-// launch or another process left -- is replaced by (tag, 1).  The arrival
-// that completes the set writes 0 back, so a CUDA-graph replay of the same
-// launch (same tag) starts from 0 as well.  The first guess is the value
-// the caller read (relaxed) while it computed its last chunk, so an arrival
-// usually takes one atomic: the last arrival of a unit is on the kernel's
-// critical path, and each failed guess costs another L2 round trip.
-// Returns 1 for the completing arrival, 0 otherwise, -1 if the swap kept
-// failing (another kernel racing on the same workspace).
+// arrivals; the arrival that completes a set writes 0 back, so a CUDA-graph
+// replay of the same launch (same tag) starts from a stale counter as well.
+// The caller passes a guess: the counter as it read it (relaxed) while it
+// computed its last chunk, or 0.  A guess carrying this launch's tag means
+// the counter keeps that tag until the set completes -- which needs this
+// arrival -- so one atomic add (acquire-release, GPU scope) counts it; the
+// later arrivals of a set, the completing one among them (on the kernel's
+// critical path), take this single L2 round trip.  Otherwise a
+// compare-and-swap replaces a counter with any other tag -- 0 after a
+// completed set, or what an earlier launch or another process left -- by
+// (tag, 1), or counts one more arrival on (tag, n), retrying with the value
+// it found.  Returns 1 for the completing arrival, 0 otherwise, -1 if the
+// swap kept failing (another kernel racing on the same workspace).
 constexpr int kArrivalBits = 20;
 __device__ __forceinline__ int arrive_on_unit(unsigned long long* ctr, unsigned long long tag,
                                               int nseg, unsigned long long guess) {
   constexpr unsigned long long kCount = (1ull << kArrivalBits) - 1;
-  const unsigned long long fresh = (tag << kArrivalBits) | 1ull;
-  unsigned long long expect = guess;
-  for (int tries = 0; tries < (1 << 20); ++tries) {
-    const unsigned long long want = (expect >> kArrivalBits) == tag ? expect + 1ull : fresh;
-    const unsigned long long seen = atomic_cas_acq_rel_gpu(ctr, expect, want);
-    if (seen == expect) {
-      const bool last = (int)(want & kCount) == nseg;
-      if (last) *reinterpret_cast<volatile unsigned long long*>(ctr) = 0ull;
-      return last ? 1 : 0;
+  unsigned long long now = 0ull;
+  if ((guess >> kArrivalBits) == tag) {
+    now = atomic_add_acq_rel_gpu_u64(ctr, 1ull) + 1ull;
+  } else {
+    const unsigned long long fresh = (tag << kArrivalBits) | 1ull;
+    unsigned long long expect = guess;
+    for (int tries = 0;; ++tries) {
+      if (tries == (1 << 20)) return -1;
+      const unsigned long long want = (expect >> kArrivalBits) == tag ? expect + 1ull : fresh;
+      const unsigned long long seen = atomic_cas_acq_rel_gpu(ctr, expect, want);
+      if (seen == expect) {
+        now = want;
+        break;
+      }
+      expect = seen;
     }
-    expect = seen;
   }
-  return -1;
+  const bool last = (int)(now & kCount) == nseg;
+  if (last) *reinterpret_cast<volatile unsigned long long*>(ctr) = 0ull;
+  return last ? 1 : 0;
 }
 
 template <int BS, int HG, int G>
@@ -1163,8 +1172,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2)
     return ngroups == 1 ? &unit_arrivals[u] : &unit_arrivals[S * ng + u + g_lo];
   };
   for (int i = 0; it.next(ch); ++i) {
-    // a split unit's last chunk in this CTA: read its arrival counter now,
-    // so the arrival after the chunk usually swaps on the first try
+    // a split unit's last chunk in this CTA: read its arrival counter now
     unsigned long long arrival_guess = 0ull;
     if (tid == 0 && ch.seg_last && !ch.whole) {
       int f, l, n, ngr, glo, ghi;

@@ -66,6 +66,13 @@ __device__ __forceinline__ unsigned long long atomic_add_acq_rel_gpu_u64(unsigne
   return old;
 }
 
+// 64-bit relaxed load at GPU scope (a hint: no ordering with other accesses).
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+
 // 64-bit compare-and-swap with release / acquire at GPU scope.
 __device__ __forceinline__ unsigned long long atomic_cas_acq_rel_gpu(unsigned long long* p,
                                                                    unsigned long long cmp,
@@ -76,13 +83,6 @@ __device__ __forceinline__ unsigned long long atomic_cas_acq_rel_gpu(unsigned lo
                : "l"(p), "l"(cmp), "l"(val)
                : "memory");
   return old;
-}
-
-// 64-bit relaxed load at GPU scope (a hint: no ordering with other accesses).
-__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
-  return v;
 }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
