@@ -37,7 +37,7 @@ import sys
 # kernel-name pattern and launches per call of each target's calls
 KERNELS = {
     "eviction": ("regex:evict_cluster", 1),  # the one-launch path (<= 16,384 blocks)
-    "attention": ("regex:decode_(stream|tc_stream|tc|fast|generic)_kernel", 1),
+    "attention": ("regex:decode_(stream|tc_stream|tcp|tc|fast|generic)_kernel", 1),
     "quantize": ("regex:quantize_bulk", 1),
     "stats": ("regex:attn_logits", 1),
 }
