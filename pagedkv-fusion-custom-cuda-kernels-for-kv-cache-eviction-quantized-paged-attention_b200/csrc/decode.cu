@@ -1650,7 +1650,19 @@ __global__ void __launch_bounds__(kCombineThreads)
   auto load_ml = [&](int s) {
     return s < n ? __ldcg(&ws_ml[slot_of(s)]) : make_float2(-INFINITY, 0.0f);
   };
+  // the (m, l) of the first 32 splits and the first kCombineDepth partial
+  // rows are requested together: one L2 round trip before the first adds
+  auto load_rows = [&](int b, int j0, int nb, float (&x)[kCombineDepth][V]) {
+#pragma unroll
+    for (int jj = 0; jj < kCombineDepth; ++jj) {
+      const float* row = ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * D + lane;
+#pragma unroll
+      for (int c = 0; c < V; ++c) x[jj][c] = __ldcg(row + 32 * c);
+    }
+  };
   const float2 ml0 = load_ml(lane);
+  float x[kCombineDepth][V];
+  load_rows(0, 0, min(32, n), x);
   float M = ml0.x;
   for (int b = 32; b < n; b += 32) M = fmaxf(M, load_ml(b + lane).x);
   M = warp_max(M);
@@ -1667,13 +1679,7 @@ __global__ void __launch_bounds__(kCombineThreads)
     }
     const int nb = min(32, n - b);
     for (int j0 = 0; j0 < nb; j0 += kCombineDepth) {
-      float x[kCombineDepth][V];
-#pragma unroll
-      for (int jj = 0; jj < kCombineDepth; ++jj) {
-        const float* row = ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * D + lane;
-#pragma unroll
-        for (int c = 0; c < V; ++c) x[jj][c] = __ldcg(row + 32 * c);
-      }
+      if (b + j0 > 0) load_rows(b, j0, nb, x);
 #pragma unroll
       for (int jj = 0; jj < kCombineDepth; ++jj) {
         const float wj = __shfl_sync(0xffffffffu, w, (j0 + jj) & 31);
