@@ -1636,6 +1636,27 @@ __global__ void __launch_bounds__(kCombineThreads)
   if (pair >= (int64_t)num_seqs * num_heads) return;  // whole warps
   const int seq = (int)(pair / num_heads);
   const int h = (int)(pair - (int64_t)seq * num_heads);
+  const int64_t base = (int64_t)seq * max_splits * num_heads + h;
+  auto slot_of = [&](int s) { return base + (int64_t)s * num_heads; };
+  auto load_rows = [&](int b, int j0, int nb, float (&x)[kCombineDepth][V]) {
+#pragma unroll
+    for (int jj = 0; jj < kCombineDepth; ++jj) {
+      const float* row = ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * D + lane;
+#pragma unroll
+      for (int c = 0; c < V; ++c) x[jj][c] = __ldcg(row + 32 * c);
+    }
+  };
+  // The (m, l) of the first 32 split slots and the first kCombineDepth
+  // partial rows are requested together with the sequence length, before
+  // the split count is known: one L2 round trip before the first adds.
+  // Slots past the count hold older contents; they are masked out below and
+  // never added.  (With one split per sequence there is no workspace.)
+  float2 ml_first = make_float2(-INFINITY, 0.0f);
+  float x[kCombineDepth][V];
+  if (max_splits > 1) {
+    ml_first = __ldcg(&ws_ml[slot_of(min(lane, max_splits - 1))]);
+    load_rows(0, 0, min(32, max_splits), x);
+  }
   const int n_pages = covered_pages(seq_lens[seq], bs, max_blocks_per_seq);
   const int n = (n_pages + pages_per_split - 1) / pages_per_split;
   float* o = out + ((int64_t)seq * num_heads + h) * D;
@@ -1645,24 +1666,10 @@ __global__ void __launch_bounds__(kCombineThreads)
     return;
   }
   if (n == 1) return;  // written by the split kernel
-  const int64_t base = (int64_t)seq * max_splits * num_heads + h;
-  auto slot_of = [&](int s) { return base + (int64_t)s * num_heads; };
   auto load_ml = [&](int s) {
     return s < n ? __ldcg(&ws_ml[slot_of(s)]) : make_float2(-INFINITY, 0.0f);
   };
-  // the (m, l) of the first 32 splits and the first kCombineDepth partial
-  // rows are requested together: one L2 round trip before the first adds
-  auto load_rows = [&](int b, int j0, int nb, float (&x)[kCombineDepth][V]) {
-#pragma unroll
-    for (int jj = 0; jj < kCombineDepth; ++jj) {
-      const float* row = ws_acc + slot_of(b + min(j0 + jj, nb - 1)) * D + lane;
-#pragma unroll
-      for (int c = 0; c < V; ++c) x[jj][c] = __ldcg(row + 32 * c);
-    }
-  };
-  const float2 ml0 = load_ml(lane);
-  float x[kCombineDepth][V];
-  load_rows(0, 0, min(32, n), x);
+  const float2 ml0 = lane < n ? ml_first : make_float2(-INFINITY, 0.0f);
   float M = ml0.x;
   for (int b = 32; b < n; b += 32) M = fmaxf(M, load_ml(b + lane).x);
   M = warp_max(M);
