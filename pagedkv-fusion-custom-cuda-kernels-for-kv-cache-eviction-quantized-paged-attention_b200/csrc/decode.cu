@@ -2100,8 +2100,10 @@ struct TcsCfg {
   static constexpr int kMaxTiles = G <= 4 ? 4 : 2;
   static constexpr int kMaxTok = kMaxTiles * kTileTok;
   static constexpr int kMaxPages = kMaxTiles * kPagesPerTile;
-  static constexpr int kStages = 3;
-  static constexpr int kMinBlocks = 3;
+  // four CTAs per SM with 2-stage rings beat three with 3-stage rings (one
+  // more unit chain per SM); groups of 8 do not fit four CTAs' shared memory
+  static constexpr int kStages = G <= 4 ? 2 : 3;
+  static constexpr int kMinBlocks = G <= 4 ? 4 : 3;
   static constexpr int kThreads = 256;
   static constexpr int kRowBytes = ((kNQ * 128 + 1023) / 1024) * 1024;
   // table halves: the query digit tiles (1 KB aligned, an MMA operand), and

@@ -343,7 +343,7 @@ def test_attention_stream_one_sequence_over_all_ctas(cuda):
 
 
 def _tc_form(monkeypatch, form):
-    """persistent: one KV head per unit, three CTAs per SM walking the units
+    """persistent: one KV head per unit, three or four CTAs per SM walking the units
     (the default); split: one CTA per split (both followed by the combine
     kernel); page: whole pages per copy, all KV heads of a sequence in one
     CTA, the stream kernel's scheduling (on request; one launch)."""
